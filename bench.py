@@ -1,0 +1,456 @@
+"""Decode hot-path benchmark (configuration 2 of the reference's headline).
+
+One step = one decode step of the sparse-attention hot path for every request
+of the rank: for each of the 32 layers, Quest page selection, the row
+resolver, the host->pool miss gather and physical-row attention, for 16
+requests per GPU (Llama-3-8B shape: 32 q / 8 KV heads, head_dim 128, bf16) at
+32,768 tokens of context with 25% of the KV pages resident in the GPU pool and
+the rest only in pinned host memory. Weak scaling: every rank decodes its own
+16 requests (requests are independent; no collective on the data path).
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+
+Prints one JSON line on rank 0. `--impl reference` times the CPU restatement
+of the reference's path (the oracle) on the host cores instead.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+import numpy as np
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "nano-hisparse_b200"))
+sys.path.insert(0, str(ROOT))
+
+METRIC = "decode tok/s at 32k ctx, 25% KV resident; miss-gather GB/s vs host-link peak"
+# configuration 2
+REQUESTS, LAYERS, CONTEXT = 16, 32, 32768
+Q_HEADS, KV_HEADS, HEAD_DIM, PAGE = 32, 8, 128, 16
+TOP_PAGES = 2048 // PAGE          # Quest budget of 2048 tokens incl. sink and tail
+HOT_ROWS = 2 * 2048               # reference default: 2 x max_union_rows
+RESIDENT_FRACTION = 0.25
+DTYPE = torch.bfloat16
+
+
+def workload_config():
+    return {
+        "workload": "config 2: Llama-3-8B-shaped sparse decode hot path (Quest select, row "
+                    "resolve, host->pool miss gather, row attention) for every layer",
+        "requests_per_gpu": REQUESTS, "layers": LAYERS, "context": CONTEXT,
+        "q_heads": Q_HEADS, "kv_heads": KV_HEADS, "head_dim": HEAD_DIM, "page_size": PAGE,
+        "quest_budget_tokens": TOP_PAGES * PAGE, "hot_rows": HOT_ROWS,
+        "resident_fraction": RESIDENT_FRACTION, "kv_dtype": "bf16", "accumulate": "fp32",
+        "queries": "N(0,1) per request, layer and step (seed 1)",
+        "kv": "N(0,1) bf16, page min/max metadata from K (seed 1)",
+        "l2": "inputs larger than L2 (about 12 GiB of metadata and KV rows read per step)",
+        "parallelism": "requests sharded over ranks, no collective on the hot path",
+    }
+
+
+def measured_peaks():
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        data = json.loads(path.read_text())
+        return float(data["hbm_gbs"]), "measured (MEASURED_PEAKS.json)"
+    return 6650.0, "fallback (6.65 TB/s)"
+
+
+# ---------------------------------------------------------------------------
+# clocks
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index, self.proc, self.path = index, None, None
+
+    def start(self):
+        out = ROOT / "gpurun_out"
+        out.mkdir(exist_ok=True)
+        self.path = out / f"clocks_rank{self.index}.csv"
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        self.proc.wait(timeout=10)
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.path.read_text().splitlines():
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx.append(float(parts[2]))
+            except ValueError:
+                continue
+            for name, flag in zip(names, parts[5:9]):
+                if flag.lower().startswith("active"):
+                    reasons.add(name)
+        return {"sm_mhz": float(np.median(sm)) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------
+# GPU arm
+# ---------------------------------------------------------------------------
+def build_workload(device, seed, log):
+    from hisparse_b200 import CacheConfig, DecodeBatch, HotConfig, RowCache
+
+    n = math.ceil(CONTEXT / PAGE)
+    hot = HotConfig(TOP_PAGES * PAGE, HOT_ROWS)
+    hot_blocks = hot.hot_blocks(PAGE)
+    resident_pages = int(round(n * RESIDENT_FRACTION))
+    units = REQUESTS * LAYERS
+    config = CacheConfig(gpu_pages=units * (resident_pages + hot_blocks), host_pages=units * n,
+                         page_size=PAGE, kv_heads=KV_HEADS, head_dim=HEAD_DIM,
+                         device=str(device), dtype=DTYPE,
+                         index_budget_bytes=1 << 40)
+    t0 = time.time()
+    host = torch.empty((config.host_pages, 2, PAGE, KV_HEADS, HEAD_DIM), dtype=DTYPE,
+                       pin_memory=True)
+    log(f"pinned host store {host.numel() * 2 / 2**30:.1f} GiB in {time.time() - t0:.1f}s")
+    cache = RowCache(config, hot, host=host)
+    gen = torch.Generator(device=device).manual_seed(seed)
+    rng = np.random.default_rng(seed)
+    mins = {r: torch.empty((LAYERS, n, KV_HEADS, HEAD_DIM), dtype=DTYPE, device=device)
+            for r in range(REQUESTS)}
+    maxs = {r: torch.empty_like(mins[r]) for r in range(REQUESTS)}
+    block = 0
+    t0 = time.time()
+    for r in range(REQUESTS):
+        for layer in range(LAYERS):
+            base = (r * LAYERS + layer) * n
+            kv = torch.randn((n, 2, PAGE, KV_HEADS, HEAD_DIM), generator=gen, device=device,
+                             dtype=torch.float32).to(DTYPE)
+            mins[r][layer] = kv[:, 0].amin(1)
+            maxs[r][layer] = kv[:, 0].amax(1)
+            host[base:base + n].copy_(kv, non_blocking=True)
+            # 25% of the pages resident: the two tail pages plus a uniform sample
+            chosen = rng.choice(n - 2, size=resident_pages - 2, replace=False)
+            pages = np.sort(np.concatenate([chosen, [n - 2, n - 1]]))
+            resident = np.full(n, -1, dtype=np.int64)
+            resident[pages] = np.arange(block, block + resident_pages)
+            idx = torch.from_numpy(pages).to(device)
+            cache.pool[block:block + resident_pages] = kv.index_select(0, idx)
+            block += resident_pages
+            hot_list = list(range(block, block + hot_blocks))
+            block += hot_blocks
+            cache.add_layer(r, layer, CONTEXT, np.arange(base, base + n), resident, hot_list)
+    torch.cuda.synchronize(device)
+    log(f"generated KV, metadata and placement in {time.time() - t0:.1f}s")
+    batch = DecodeBatch(cache, list(range(REQUESTS)), LAYERS, mins, maxs, TOP_PAGES, Q_HEADS)
+    return cache, batch
+
+
+def bytes_per_unit(valid_rows, misses):
+    """Algorithmic HBM bytes of one (request, layer): Quest metadata (min+max),
+    K+V of every selected row, and the miss rows written into the pool."""
+    row = 2 * KV_HEADS * HEAD_DIM * 2
+    meta = 2 * math.ceil(CONTEXT / PAGE) * KV_HEADS * HEAD_DIM * 2
+    return meta + valid_rows * row + misses * row
+
+
+def hostlink_peak(device):
+    """Measured pinned host->device copy bandwidth (copy engine), GB/s."""
+    nbytes = 1 << 30
+    src = torch.empty(nbytes, dtype=torch.uint8, pin_memory=True)
+    dst = torch.empty(nbytes, dtype=torch.uint8, device=device)
+    best = float("inf")
+    for _ in range(5):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        dst.copy_(src, non_blocking=True)
+        b.record()
+        torch.cuda.synchronize(device)
+        best = min(best, a.elapsed_time(b))
+    del src, dst
+    return nbytes / best / 1e6
+
+
+def run_gpu(args, rank, world, local_rank, log):
+    import torch.distributed as dist
+
+    from hisparse_b200 import _lib
+
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    hbm_peak, hbm_source = measured_peaks()
+    link_peak = hostlink_peak(device)
+    cache, batch = build_workload(device, 1 + rank, log)
+    steps, warmup = args.steps, args.warmup
+    gen = torch.Generator(device=device).manual_seed(1000 + rank)
+    total = steps + warmup
+    queries = torch.randn((total, LAYERS, REQUESTS, Q_HEADS, HEAD_DIM), generator=gen,
+                          device=device, dtype=torch.float32).to(DTYPE)
+    outs = torch.empty((LAYERS, REQUESTS, Q_HEADS, HEAD_DIM), dtype=DTYPE, device=device)
+    counts = torch.zeros((total, LAYERS, REQUESTS, 3), dtype=torch.int64, device=device)
+    compute = cache.compute
+
+    def barrier():
+        torch.cuda.synchronize(device)
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(value):
+        if world == 1:
+            return value
+        t = torch.tensor([value], dtype=torch.float64, device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    for s in range(warmup):
+        for layer in range(LAYERS):
+            batch.layer(layer, queries[s, layer], outs[layer], counts[s, layer])
+    barrier()
+    sampler = ClockSampler(local_rank)
+    sampler.start()
+    timing = []
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    start.record(compute)
+    for s in range(warmup, total):
+        for layer in range(LAYERS):
+            batch.layer(layer, queries[s, layer], outs[layer], counts[s, layer], timing)
+    end.record(compute)
+    barrier()
+    clocks = sampler.stop()
+    elapsed_ms = max_over_ranks(start.elapsed_time(end))
+
+    # per-kernel device time over the timed region (events on each launch's stream)
+    per_kernel = {}
+    for name, a, b in timing:
+        per_kernel.setdefault(name, []).append(a.elapsed_time(b))
+    kernel_ms = {k: float(np.sum(v)) for k, v in per_kernel.items()}
+    launches = {k: len(v) for k, v in per_kernel.items()}
+    timed_counts = counts[warmup:].cpu().numpy()  # [steps, L, B, 3]
+    misses = int(timed_counts[..., 2].sum())
+    valid_rows = int(timed_counts.sum())
+    row_bytes = 2 * KV_HEADS * HEAD_DIM * 2
+    gather_bytes = misses * row_bytes
+    gather_gbs = gather_bytes / (kernel_ms["gather"] * 1e-3) / 1e9
+    hbm_bytes = sum(bytes_per_unit(int(timed_counts[s, l, b].sum()), int(timed_counts[s, l, b, 2]))
+                    for s in range(steps) for l in range(LAYERS) for b in range(REQUESTS))
+    attend_bytes = valid_rows * row_bytes
+    attend_gbs = attend_bytes / (kernel_ms["attend"] * 1e-3) / 1e9
+    meta_bytes = steps * LAYERS * REQUESTS * 2 * math.ceil(CONTEXT / PAGE) * KV_HEADS * \
+        HEAD_DIM * 2
+    quest_gbs = meta_bytes / (kernel_ms["quest"] * 1e-3) / 1e9
+    t_roof = max(hbm_bytes / (hbm_peak * 1e9), gather_bytes / (link_peak * 1e9))
+    step_frac = t_roof / (elapsed_ms * 1e-3)
+
+    # ---- end to end through the public API with host buffers ------------------------
+    host_q = queries.cpu().pin_memory()
+    host_out = torch.empty((total, LAYERS, REQUESTS, Q_HEADS, HEAD_DIM), dtype=DTYPE,
+                           pin_memory=True)
+    dev_q = torch.empty((LAYERS, REQUESTS, Q_HEADS, HEAD_DIM), dtype=DTYPE, device=device)
+    for s in range(warmup):
+        for layer in range(LAYERS):
+            dev_q[layer].copy_(host_q[s, layer], non_blocking=True)
+            batch.layer(layer, dev_q[layer], outs[layer])
+            host_out[s, layer].copy_(outs[layer], non_blocking=True)
+    barrier()
+    e2e_start = torch.cuda.Event(enable_timing=True)
+    e2e_end = torch.cuda.Event(enable_timing=True)
+    e2e_start.record(compute)
+    for s in range(warmup, total):
+        for layer in range(LAYERS):
+            dev_q[layer].copy_(host_q[s, layer], non_blocking=True)
+            batch.layer(layer, dev_q[layer], outs[layer])
+            host_out[s, layer].copy_(outs[layer], non_blocking=True)
+    e2e_end.record(compute)
+    barrier()
+    e2e_ms = max_over_ranks(e2e_start.elapsed_time(e2e_end))
+    flags = _lib.device_flags(device)
+    if flags:
+        raise RuntimeError(f"device flags raised during the bench: {flags}")
+
+    tokens = REQUESTS * steps * world
+    value = tokens / (elapsed_ms * 1e-3)
+    io_bytes = LAYERS * REQUESTS * Q_HEADS * HEAD_DIM * 2
+    result = {
+        "metric": METRIC, "value": round(value, 2), "unit": "tok/s", "n_gpus": world,
+        "steps": steps, "warmup": warmup, "ms_per_step": round(elapsed_ms / steps, 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic", "config": workload_config(),
+        "e2e": {"value": round(tokens / (e2e_ms * 1e-3), 2), "unit": "tok/s",
+                "h2d_bytes_per_step": io_bytes, "d2h_bytes_per_step": io_bytes},
+        "gpu_launches": int(sum(launches.values()) + launches["quest"] + launches["attend"]),
+        "roofline": {
+            "kernel": "gather_kernel (host->pool miss gather)", "bound": "hostlink",
+            "achieved": round(gather_gbs, 2),
+            "peak": round(link_peak, 2), "unit": "GB/s", "frac": round(gather_gbs / link_peak, 4),
+            "peak_source": "measured in bench.py: pinned host->device cudaMemcpyAsync, 1 GiB",
+            "traffic": None,
+            "bytes_per_launch": round(gather_bytes / launches["gather"]),
+            "ms_per_launch": round(kernel_ms["gather"] / launches["gather"], 4),
+        },
+        "roofline_hbm": {
+            "attend_kernel": {"achieved": round(attend_gbs, 1), "peak": hbm_peak,
+                              "frac": round(attend_gbs / hbm_peak, 4), "unit": "GB/s",
+                              "peak_source": hbm_source,
+                              "ms_per_launch": round(kernel_ms["attend"] / launches["attend"], 4)},
+            "quest_kernels": {"achieved": round(quest_gbs, 1), "peak": hbm_peak,
+                              "frac": round(quest_gbs / hbm_peak, 4), "unit": "GB/s",
+                              "peak_source": hbm_source,
+                              "ms_per_launch": round(kernel_ms["quest"] / launches["quest"], 4)},
+            "resolve_ms_per_launch": round(kernel_ms["resolve"] / launches["resolve"], 4),
+        },
+        "step_roofline": {
+            "definition": "t_roof = max(HBM bytes / HBM peak, miss bytes / host-link peak)",
+            "hbm_bytes_per_step": int(hbm_bytes / steps),
+            "hostlink_bytes_per_step": int(gather_bytes / steps), "t_roof_ms": round(
+                t_roof * 1e3 / steps, 3), "frac": round(step_frac, 4)},
+        "resolver": {"resident_hits": int(timed_counts[..., 0].sum()),
+                     "hot_hits": int(timed_counts[..., 1].sum()), "misses": misses,
+                     "miss_rows_per_unit": round(misses / (steps * LAYERS * REQUESTS), 1)},
+        "kernel_ms_per_step": {k: round(v / steps, 3) for k, v in kernel_ms.items()},
+        "clocks": clocks,
+    }
+    return result
+
+
+# ---------------------------------------------------------------------------
+# CPU arm (oracle restatement of the reference's path)
+# ---------------------------------------------------------------------------
+def cpu_sample(seed=1, budget_s=10.0, threads=None, log=print):
+    """Times oracle.decode_layer_batched — the whole per-(request, layer) hot
+    path, OpenMP over the 16 requests — on the host cores for one layer at a
+    time, and extrapolates to tok/s over 32 layers."""
+    import oracle
+
+    threads = threads or os.cpu_count() or 1
+    n = math.ceil(CONTEXT / PAGE)
+    hot_blocks = math.ceil(HOT_ROWS / PAGE)
+    resident_pages = int(round(n * RESIDENT_FRACTION))
+    rng = np.random.default_rng(seed)
+    t0 = time.time()
+    host = torch.empty((REQUESTS * n, 2, PAGE, KV_HEADS, HEAD_DIM), dtype=DTYPE)
+
+    def fill(r):  # one request's pages per task; torch releases the GIL
+        gen = torch.Generator().manual_seed(seed * 1000 + r)
+        host[r * n:(r + 1) * n] = torch.randn(host[r * n:(r + 1) * n].shape, generator=gen)
+
+    from concurrent.futures import ThreadPoolExecutor
+
+    with ThreadPoolExecutor(max_workers=threads) as pool_exec:
+        list(pool_exec.map(fill, range(REQUESTS)))
+    pool = torch.zeros((REQUESTS * (resident_pages + hot_blocks), 2, PAGE, KV_HEADS, HEAD_DIM),
+                       dtype=DTYPE)
+    queries, mins, maxs, sources, residents, hots, tags, lrus = ([] for _ in range(8))
+    block = 0
+    for r in range(REQUESTS):
+        base = r * n
+        keys = host[base:base + n, 0].float()
+        mins.append(keys.amin(1).to(DTYPE))
+        maxs.append(keys.amax(1).to(DTYPE))
+        chosen = rng.choice(n - 2, size=resident_pages - 2, replace=False)
+        pages = np.sort(np.concatenate([chosen, [n - 2, n - 1]]))
+        resident = np.full(n, -1, dtype=np.int64)
+        resident[pages] = np.arange(block, block + resident_pages)
+        pool[block:block + resident_pages] = host[base + pages]
+        block += resident_pages
+        hots.append(np.arange(block, block + hot_blocks, dtype=np.int64))
+        block += hot_blocks
+        sources.append(np.arange(base, base + n, dtype=np.int64))
+        residents.append(resident)
+        tags.append(np.full(HOT_ROWS, -1, dtype=np.int64))
+        lrus.append(np.arange(HOT_ROWS, dtype=np.int64))
+    log(f"cpu sample data in {time.time() - t0:.1f}s")
+    host_np = host.view(torch.int16).numpy()
+    pool_np = pool.view(torch.int16).numpy()
+    times = []
+    t_start = time.time()
+    it = 0
+    while it < 2 or (time.time() - t_start < budget_s and it < 64):
+        qgen = torch.Generator().manual_seed(seed * 7919 + it)
+        qs = [torch.randn((Q_HEADS, HEAD_DIM), generator=qgen).to(DTYPE) for _ in range(REQUESTS)]
+        a = time.perf_counter()
+        oracle.decode_layer_batched(qs, mins, maxs, [CONTEXT] * REQUESTS, PAGE, TOP_PAGES, n,
+                                    sources, residents, hots, tags, lrus, host_np, pool_np,
+                                    threads=threads)
+        times.append(time.perf_counter() - a)
+        it += 1
+    per_layer = float(np.mean(times[1:])) if len(times) > 1 else times[0]
+    value = REQUESTS / (per_layer * LAYERS)
+    return {
+        "value": round(value, 4), "unit": "tok/s", "cores": threads, "kind": "port",
+        "sample": f"{len(times)} layer passes of {REQUESTS} requests (first untimed warm-up), "
+                  f"{per_layer * 1e3:.1f} ms per layer, extrapolated x{LAYERS} layers; oracle "
+                  "restatement in C (OpenMP over requests; fp64 attention)",
+    }
+
+
+def main():
+    parser = argparse.ArgumentParser(description=__doc__.split("\n\n")[0])
+    parser.add_argument("--gpus", type=int, default=1)
+    parser.add_argument("--steps", type=int, default=10)
+    parser.add_argument("--warmup", type=int, default=3)
+    parser.add_argument("--impl", default="hisparse_b200", choices=["hisparse_b200", "reference"])
+    parser.add_argument("--no-cpu-baseline", action="store_true")
+    args = parser.parse_args()
+    rank = int(os.environ.get("RANK", 0))
+    world = int(os.environ.get("WORLD_SIZE", 1))
+    local_rank = int(os.environ.get("LOCAL_RANK", 0))
+
+    def log(msg):
+        if rank == 0:
+            print(f"[bench] {msg}", file=sys.stderr, flush=True)
+
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        base = cpu_sample(log=log)
+        line = {"metric": METRIC, "value": base["value"], "unit": "tok/s", "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+                "config": workload_config(), "impl": "reference", "cpu_baseline": base,
+                "e2e": {"value": base["value"], "unit": "tok/s", "h2d_bytes_per_step": 0,
+                        "d2h_bytes_per_step": 0}}
+        print(json.dumps(line), flush=True)
+        return
+
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                device_id=torch.device("cuda", local_rank))
+    try:
+        result = run_gpu(args, rank, world, local_rank, log)
+        if rank == 0:
+            if world == 1 and not args.no_cpu_baseline:
+                result["cpu_baseline"] = cpu_sample(log=log)
+            print(json.dumps(result), flush=True)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

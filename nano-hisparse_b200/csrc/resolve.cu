@@ -1,0 +1,528 @@
+// (2) Row resolver: resident lookup, hot-tag lookup, LRU replacement and the
+// compact miss plan, with the in-place tag/LRU update.
+//
+// Reference: nano_hisparse/row_index.py:62-140 (resolve_rows). The reference
+// expresses the algorithm as ~35 tensor ops (sorts, searchsorted, argsorts,
+// scatters). Here one CTA of 1024 threads resolves one request:
+//   1. bitonic sort of the normalised logical positions;
+//   2. per sorted entry: dedupe, page -> (host row, resident block) lookup;
+//   3. open-addressing hash of the hot tags (tag -> slot) shared by the hot-hit
+//      lookup and the "protect every hit" pass;
+//   4. block scans give each miss its rank (sorted logical order) and each
+//      unprotected slot its victim rank (LRU order), so miss r takes victim r;
+//   5. a stable 4-way partition of the old LRU order by category
+//      (untouched, inserted, protected, inserted+protected) is the new LRU;
+//   6. inputs map back to their first occurrence in input order.
+// Per-request scratch lives in shared memory when it fits, else in the
+// caller's workspace (L2-resident); the code is the same through generic
+// pointers. No host round trip: the launch is graph-capturable.
+#include <cstdio>
+
+#include "common.cuh"
+
+namespace hs {
+namespace {
+
+constexpr int kResolveThreads = 1024;
+constexpr size_t kResolveSmemLimit = 200 * 1024;
+constexpr unsigned long long kEmpty = ~0ull;
+constexpr unsigned long long kWantedBit = 1ull << 31;
+
+enum : uint8_t {
+  kValid = 1,        // unique, in range, and source page >= 0
+  kResidentHit = 2,  // valid and resident block >= 0
+  kNeedsHot = 4,     // valid and not resident
+  kHotHit = 8,       // needs hot and its host row is tagged
+  kMiss = 16         // needs hot and not tagged
+};
+enum : uint8_t { kProtected = 1, kInserted = 2 };
+
+__host__ __device__ inline int64_t next_pow2(int64_t x) {
+  int64_t p = 1;
+  while (p < x) p <<= 1;
+  return p;
+}
+
+__host__ __device__ inline size_t align16(size_t x) { return (x + 15) & ~size_t(15); }
+
+struct Layout {
+  int64_t kp, ch;  // padded sort length, hash capacity
+  size_t keys, first, flags, slot, host, phys, hash, sflags, lru_old, victims, total;
+  __host__ __device__ Layout(int64_t k, int64_t h) {
+    kp = next_pow2(k);
+    ch = next_pow2(2 * h);
+    if (ch < 64) ch = 64;
+    size_t o = 0;
+    keys = o;    o = align16(o + kp * 4);
+    first = o;   o = align16(o + k * 4);
+    flags = o;   o = align16(o + k);
+    slot = o;    o = align16(o + k * 4);
+    host = o;    o = align16(o + k * 8);
+    phys = o;    o = align16(o + k * 8);
+    hash = o;    o = align16(o + ch * 8);
+    sflags = o;  o = align16(o + h);
+    lru_old = o; o = align16(o + h * 4);
+    victims = o; o = align16(o + h * 4);
+    total = o;
+  }
+};
+
+struct ResolveParams {
+  int batch;
+  const void *positions;  // [batch, count] int32 or int64
+  int positions_i64;
+  int64_t count;
+  Batched<int32_t> source, resident, hot;
+  BatchedMut<int32_t> tags;
+  BatchedMut<int64_t> lru;
+  int64_t table_pages, hot_blocks, hot_rows;
+  Lengths lengths;
+  int page_size;
+  int64_t *out_physical, *out_miss_host, *out_miss_device, *out_counts;
+  const int64_t *head_columns;
+  int64_t head_count, head_width;
+  int64_t *out_head_physical;
+  char *workspace;  // nullptr -> shared memory
+  int32_t *status;
+};
+
+__device__ __forceinline__ uint32_t hash_slot(uint32_t key, int64_t ch) {
+  return (uint32_t)((key * 0x9E3779B1u) & (uint32_t)(ch - 1));
+}
+
+__device__ __forceinline__ void hash_insert(unsigned long long *table, int64_t ch,
+                                            uint32_t key, uint32_t slot) {
+  const unsigned long long entry = ((unsigned long long)key << 32) | slot;
+  uint32_t h = hash_slot(key, ch);
+  while (true) {
+    unsigned long long cur = table[h];
+    if (cur == kEmpty) {
+      cur = atomicCAS(&table[h], kEmpty, entry);
+      if (cur == kEmpty) return;
+    }
+    if ((uint32_t)(cur >> 32) == key) {
+      atomicMin(&table[h], entry);  // duplicate tags: keep the lowest slot
+      return;
+    }
+    h = (h + 1) & (uint32_t)(ch - 1);
+  }
+}
+
+__device__ __forceinline__ int64_t hash_find(const unsigned long long *table, int64_t ch,
+                                             uint32_t key) {
+  uint32_t h = hash_slot(key, ch);
+  while (true) {
+    const unsigned long long cur = table[h];
+    if (cur == kEmpty) return -1;
+    if ((uint32_t)(cur >> 32) == key) return h;
+    h = (h + 1) & (uint32_t)(ch - 1);
+  }
+}
+
+__device__ __forceinline__ int64_t load_position(const ResolveParams &p, int b, int64_t i) {
+  const int64_t idx = (int64_t)b * p.count + i;
+  return p.positions_i64 ? static_cast<const int64_t *>(p.positions)[idx]
+                         : (int64_t) static_cast<const int32_t *>(p.positions)[idx];
+}
+
+// Smallest j in [0, n) with keys[j] >= v (n if none).
+__device__ __forceinline__ int64_t lower_bound(const int32_t *keys, int64_t n, int64_t v) {
+  int64_t lo = 0, hi = n;
+  while (lo < hi) {
+    const int64_t mid = (lo + hi) >> 1;
+    if ((int64_t)keys[mid] < v) lo = mid + 1; else hi = mid;
+  }
+  return lo;
+}
+
+__global__ void __launch_bounds__(kResolveThreads) resolve_kernel(ResolveParams p) {
+  extern __shared__ __align__(16) char smem_raw[];
+  __shared__ int64_t scan_scratch[33];
+  __shared__ int s_abort;
+  __shared__ unsigned long long s_counts[3];
+  const int b = blockIdx.x;
+  const int tid = threadIdx.x, nthreads = blockDim.x;
+  const int64_t K = p.count, H = p.hot_rows;
+  const Layout L(K, H);
+  char *base = p.workspace ? p.workspace + (size_t)b * L.total : smem_raw;
+  int32_t *keys = reinterpret_cast<int32_t *>(base + L.keys);
+  int32_t *first_in = reinterpret_cast<int32_t *>(base + L.first);
+  uint8_t *jflags = reinterpret_cast<uint8_t *>(base + L.flags);
+  int32_t *jslot = reinterpret_cast<int32_t *>(base + L.slot);
+  int64_t *jhost = reinterpret_cast<int64_t *>(base + L.host);
+  int64_t *jphys = reinterpret_cast<int64_t *>(base + L.phys);
+  unsigned long long *table = reinterpret_cast<unsigned long long *>(base + L.hash);
+  uint8_t *sflags = reinterpret_cast<uint8_t *>(base + L.sflags);
+  int32_t *lru_old = reinterpret_cast<int32_t *>(base + L.lru_old);
+  int32_t *victims = reinterpret_cast<int32_t *>(base + L.victims);
+
+  const int32_t *src_tab = p.source.at(b);
+  const int32_t *res_tab = p.resident.at(b);
+  const int32_t *hot_tab = p.hot.at(b);
+  int32_t *tags = p.tags.at(b);
+  int64_t *lru = p.lru.at(b);
+  const int64_t length = p.lengths.at(b);
+  const int P = p.page_size;
+  int64_t *out_phys = p.out_physical + (int64_t)b * K;
+  int64_t *out_mh = p.out_miss_host + (int64_t)b * K;
+  int64_t *out_md = p.out_miss_device + (int64_t)b * K;
+  int64_t *out_counts = p.out_counts + (int64_t)b * 3;
+
+  if (tid == 0) {
+    s_abort = 0;
+    s_counts[0] = s_counts[1] = s_counts[2] = 0;
+  }
+  // ---- 1. load and normalise; clear scratch -----------------------------------
+  for (int64_t i = tid; i < L.kp; i += nthreads) {
+    int32_t v = INT32_MAX;
+    if (i < K) {
+      const int64_t raw = load_position(p, b, i);
+      v = (int32_t)((raw >= 0 && raw < length) ? raw : length);
+      first_in[i] = (int32_t)K;
+    }
+    keys[i] = v;
+  }
+  for (int64_t s = tid; s < L.ch; s += nthreads) table[s] = kEmpty;
+  __syncthreads();
+  for (int64_t s = tid; s < H; s += nthreads) {
+    sflags[s] = 0;
+    const int64_t v = lru[s];
+    if (v < 0 || v >= H) s_abort = 1;
+    lru_old[s] = (int32_t)v;
+  }
+  // ---- 2. bitonic sort of keys[0, kp) ascending ---------------------------------
+  for (int64_t k = 2; k <= L.kp; k <<= 1) {
+    for (int64_t j = k >> 1; j > 0; j >>= 1) {
+      __syncthreads();
+      for (int64_t i = tid; i < L.kp; i += nthreads) {
+        const int64_t l = i ^ j;
+        if (l > i) {
+          const int32_t a = keys[i], c = keys[l];
+          const bool up = (i & k) == 0;
+          if ((a > c) == up) {
+            keys[i] = c;
+            keys[l] = a;
+          }
+        }
+      }
+    }
+  }
+  __syncthreads();
+  if (s_abort) {
+    // A corrupt LRU permutation cannot be resolved faithfully: leave the
+    // tables untouched and return an empty plan.
+    for (int64_t i = tid; i < K; i += nthreads) out_phys[i] = out_mh[i] = out_md[i] = -1;
+    if (tid < 3) out_counts[tid] = 0;
+    if (tid == 0) flag(p.status, HS_DEV_LRU_CORRUPT);
+    goto head_columns;
+  }
+  // ---- 3. first occurrence in input order; per-entry lookups; tag hash ---------
+  for (int64_t i = tid; i < K; i += nthreads) {
+    const int64_t raw = load_position(p, b, i);
+    if (raw >= 0 && raw < length) atomicMin(&first_in[lower_bound(keys, K, raw)], (int32_t)i);
+  }
+  for (int64_t j = tid; j < K; j += nthreads) {
+    const int64_t v = keys[j];
+    const bool unique = v < length && (j == 0 || keys[j - 1] != keys[j]);
+    int64_t page = v / P;
+    if (page > p.table_pages - 1) page = p.table_pages - 1;
+    const int64_t offset = v % P;
+    const int64_t source = src_tab[page];
+    const int64_t resident = res_tab[page];
+    const int64_t host = source * P + offset;
+    uint8_t f = 0;
+    int64_t phys = -1;
+    if (unique && source >= 0) {
+      f |= kValid;
+      if (resident >= 0) {
+        f |= kResidentHit;
+        phys = resident * P + offset;
+      } else {
+        f |= kNeedsHot;
+      }
+    }
+    jflags[j] = f;
+    jhost[j] = host;
+    jphys[j] = phys;
+  }
+  for (int64_t s = tid; s < H; s += nthreads) {
+    const int32_t t = tags[s];
+    if (t >= 0) hash_insert(table, L.ch, (uint32_t)t, (uint32_t)s);
+  }
+  __syncthreads();
+  // ---- 4. hot-hit lookup; mark wanted tags ---------------------------------------
+  for (int64_t j = tid; j < K; j += nthreads) {
+    uint8_t f = jflags[j];
+    if (f & kNeedsHot) {
+      const int64_t host = jhost[j];
+      int64_t at = -1;
+      if (host >= 0 && host <= INT32_MAX) at = hash_find(table, L.ch, (uint32_t)host);
+      if (at >= 0) {
+        f |= kHotHit;
+        jslot[j] = (int32_t)(table[at] & 0x7fffffffu);
+        atomicOr(&table[at], kWantedBit);
+      } else {
+        f |= kMiss;
+      }
+      jflags[j] = f;
+    }
+  }
+  __syncthreads();
+  // ---- 5. protected slots; miss ranks (sorted logical order) --------------------
+  for (int64_t s = tid; s < H; s += nthreads) {
+    const int32_t t = tags[s];
+    if (t >= 0) {
+      const int64_t at = hash_find(table, L.ch, (uint32_t)t);
+      if (at >= 0 && (table[at] & kWantedBit)) sflags[s] = kProtected;
+    }
+  }
+  int64_t misses;
+  {
+    const int64_t per = ceil_div(K, nthreads);
+    const int64_t lo = min(K, tid * per), hi = min(K, lo + per);
+    int64_t local = 0;
+    for (int64_t j = lo; j < hi; ++j) local += (jflags[j] & kMiss) != 0;
+    int64_t rank = block_exclusive_scan<int64_t>(local, scan_scratch, &misses);
+    for (int64_t j = lo; j < hi; ++j)
+      if (jflags[j] & kMiss) jslot[j] = (int32_t)(rank++);  // temporarily the miss rank
+  }
+  // ---- 6. victims: unprotected slots in LRU order, then protected ----------------
+  {
+    const int64_t per = ceil_div(H, nthreads);
+    const int64_t lo = min(H, tid * per), hi = min(H, lo + per);
+    int64_t local = 0;
+    for (int64_t i = lo; i < hi; ++i) local += !(sflags[lru_old[i]] & kProtected);
+    int64_t unprotected;
+    int64_t pos = block_exclusive_scan<int64_t>(local, scan_scratch, &unprotected);
+    for (int64_t i = lo; i < hi; ++i) {
+      const int32_t s = lru_old[i];
+      if (!(sflags[s] & kProtected)) victims[pos++] = s;
+      else victims[unprotected + (i - pos)] = s;
+    }
+  }
+  __syncthreads();
+  if (misses > H) {
+    // Only reachable with more positions than hot rows (the cache caps
+    // positions at max_union_rows <= hot_rows).
+    for (int64_t i = tid; i < K; i += nthreads) out_phys[i] = out_mh[i] = out_md[i] = -1;
+    if (tid < 3) out_counts[tid] = 0;
+    if (tid == 0) flag(p.status, HS_DEV_MISSES_EXCEED_HOT);
+    goto head_columns;
+  }
+  // ---- 7. slots, physical rows, miss plan, tag update -----------------------------
+  {
+    unsigned long long c_res = 0, c_hot = 0, c_miss = 0;
+    for (int64_t j = tid; j < K; j += nthreads) {
+      const uint8_t f = jflags[j];
+      c_res += (f & kResidentHit) != 0;
+      if (!(f & kNeedsHot)) continue;
+      int32_t slot;
+      if (f & kMiss) {
+        const int32_t rank = jslot[j];
+        slot = victims[rank];
+        jslot[j] = slot;
+        sflags[slot] |= kInserted;
+        ++c_miss;
+      } else {
+        slot = jslot[j];
+        ++c_hot;
+      }
+      const int64_t block = hot_tab[slot / P];
+      const int64_t hot_phys = block * P + slot % P;
+      jphys[j] = hot_phys;
+    }
+    atomicAdd(&s_counts[0], c_res);
+    atomicAdd(&s_counts[1], c_hot);
+    atomicAdd(&s_counts[2], c_miss);
+  }
+  __syncthreads();
+  {
+    // Miss plan: the miss ranks were consumed above, so rebuild them with the
+    // same scan (deterministic) and write entries in sorted logical order.
+    const int64_t per = ceil_div(K, nthreads);
+    const int64_t lo = min(K, tid * per), hi = min(K, lo + per);
+    int64_t local = 0;
+    for (int64_t j = lo; j < hi; ++j) local += (jflags[j] & kMiss) != 0;
+    int64_t total;
+    int64_t rank = block_exclusive_scan<int64_t>(local, scan_scratch, &total);
+    for (int64_t j = lo; j < hi; ++j) {
+      if (jflags[j] & kMiss) {
+        out_mh[rank] = jhost[j];
+        out_md[rank] = jphys[j];
+        tags[jslot[j]] = (int32_t)jhost[j];
+        ++rank;
+      }
+    }
+    for (int64_t i = total + tid; i < K; i += nthreads) out_mh[i] = out_md[i] = -1;
+  }
+  if (tid < 3) out_counts[tid] = (int64_t)s_counts[tid];
+  __syncthreads();
+  // ---- 8. new LRU: stable partition by category of the old order ------------------
+  {
+    const int64_t per = ceil_div(H, nthreads);
+    const int64_t lo = min(H, tid * per), hi = min(H, lo + per);
+    int64_t c01 = 0, c23 = 0;  // two 32-bit counters per 64-bit word
+    for (int64_t i = lo; i < hi; ++i) {
+      const uint8_t f = sflags[lru_old[i]];
+      const int cat = ((f & kInserted) ? 1 : 0) + ((f & kProtected) ? 2 : 0);
+      if (cat < 2) c01 += (int64_t)1 << (32 * cat);
+      else c23 += (int64_t)1 << (32 * (cat - 2));
+    }
+    int64_t t01, t23;
+    const int64_t e01 = block_exclusive_scan<int64_t>(c01, scan_scratch, &t01);
+    const int64_t e23 = block_exclusive_scan<int64_t>(c23, scan_scratch, &t23);
+    const int64_t tot0 = t01 & 0xffffffff, tot1 = t01 >> 32, tot2 = t23 & 0xffffffff;
+    int64_t pos[4] = {e01 & 0xffffffff, tot0 + (e01 >> 32), tot0 + tot1 + (e23 & 0xffffffff),
+                      tot0 + tot1 + tot2 + (e23 >> 32)};
+    for (int64_t i = lo; i < hi; ++i) {
+      const int32_t s = lru_old[i];
+      const uint8_t f = sflags[s];
+      const int cat = ((f & kInserted) ? 1 : 0) + ((f & kProtected) ? 2 : 0);
+      lru[pos[cat]++] = s;
+    }
+  }
+  // ---- 9. results in input order ------------------------------------------------------
+  for (int64_t i = tid; i < K; i += nthreads) {
+    const int64_t raw = load_position(p, b, i);
+    int64_t r = -1;
+    if (raw >= 0 && raw < length) {
+      const int64_t f = lower_bound(keys, K, raw);
+      if (first_in[f] == (int32_t)i) r = jphys[f];
+    }
+    out_phys[i] = r;
+  }
+head_columns:
+  if (p.head_columns != nullptr) {
+    __syncthreads();
+    const int64_t n = p.head_count * p.head_width;
+    for (int64_t i = tid; i < n; i += nthreads) {
+      const int64_t c = p.head_columns[i];
+      p.out_head_physical[i] = (c >= 0 && c < K) ? out_phys[c] : -1;
+    }
+  }
+}
+
+int resolve_common(ResolveParams &p, size_t workspace_bytes, cudaStream_t stream) {
+  if (p.batch < 1 || p.count < 1 || p.hot_rows < 1 || p.page_size < 1 || p.table_pages < 1)
+    return set_error(HS_ERR_INVALID_ARGUMENT, "resolve: dimensions must be positive");
+  if (p.count > INT32_MAX || p.hot_rows > INT32_MAX)
+    return set_error(HS_ERR_INVALID_ARGUMENT, "resolve: count and hot_rows must fit int32");
+  if (p.hot_blocks * (int64_t)p.page_size < p.hot_rows)
+    return set_error(HS_ERR_INVALID_ARGUMENT,
+                     "resolve: hot table of %lld blocks cannot address %lld hot rows",
+                     (long long)p.hot_blocks, (long long)p.hot_rows);
+  if (!p.positions || !p.out_physical || !p.out_miss_host || !p.out_miss_device ||
+      !p.out_counts)
+    return set_error(HS_ERR_INVALID_ARGUMENT, "resolve: null tensor pointer");
+  if (p.head_columns && (!p.out_head_physical || p.head_count < 1 || p.head_width < 1))
+    return set_error(HS_ERR_INVALID_ARGUMENT, "resolve: invalid head columns");
+  const Layout L(p.count, p.hot_rows);
+  size_t smem = 0;
+  if (L.total <= kResolveSmemLimit) {
+    smem = L.total;
+    p.workspace = nullptr;
+  } else {
+    const size_t need = hs_resolve_workspace_bytes(p.batch, p.count, p.hot_rows);
+    if (!p.workspace || workspace_bytes < need)
+      return set_error(HS_ERR_WORKSPACE, "resolve: workspace of %zu bytes < required %zu",
+                       workspace_bytes, need);
+  }
+  if (smem > 48 * 1024 &&
+      cudaFuncSetAttribute(resolve_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)smem) != cudaSuccess)
+    return set_error(HS_ERR_CUDA, "resolve: cannot reserve %zu bytes of shared memory", smem);
+  resolve_kernel<<<p.batch, kResolveThreads, smem, stream>>>(p);
+  return check_launch("resolve_kernel");
+}
+
+}  // namespace
+}  // namespace hs
+
+extern "C" size_t hs_resolve_workspace_bytes(int batch, int64_t count, int64_t hot_rows) {
+  if (batch < 1 || count < 1 || hot_rows < 1) return 0;
+  const hs::Layout L(count, hot_rows);
+  if (L.total <= hs::kResolveSmemLimit) return 0;
+  return (size_t)batch * L.total;
+}
+
+extern "C" int hs_resolve_rows(const void *positions, int positions_dtype, int64_t count,
+                               const int32_t *source_table, const int32_t *resident_table,
+                               int64_t table_pages, const int32_t *hot_table,
+                               int64_t hot_blocks, int32_t *tags, int64_t *lru,
+                               int64_t hot_rows, int64_t length, int page_size,
+                               int64_t *out_physical, int64_t *out_miss_host,
+                               int64_t *out_miss_device, int64_t *out_counts,
+                               const int64_t *head_columns, int64_t head_count,
+                               int64_t head_width, int64_t *out_head_physical,
+                               void *workspace, size_t workspace_bytes,
+                               int32_t *device_status, hs_stream stream) {
+  if (positions_dtype != HS_INT32 && positions_dtype != HS_INT64)
+    return hs::set_error(HS_ERR_INVALID_ARGUMENT, "resolve: positions must be int32 or int64");
+  if (!source_table || !resident_table || !hot_table || !tags || !lru)
+    return hs::set_error(HS_ERR_INVALID_ARGUMENT, "resolve: null table pointer");
+  if (length < 0 || length > INT32_MAX)
+    return hs::set_error(HS_ERR_INVALID_ARGUMENT, "resolve: length must be in [0, 2^31)");
+  hs::ResolveParams p{};
+  p.batch = 1;
+  p.positions = positions;
+  p.positions_i64 = positions_dtype == HS_INT64;
+  p.count = count;
+  p.source = {source_table, 0, nullptr};
+  p.resident = {resident_table, 0, nullptr};
+  p.hot = {hot_table, 0, nullptr};
+  p.tags = {tags, 0, nullptr};
+  p.lru = {lru, 0, nullptr};
+  p.table_pages = table_pages;
+  p.hot_blocks = hot_blocks;
+  p.hot_rows = hot_rows;
+  p.lengths = {nullptr, length};
+  p.page_size = page_size;
+  p.out_physical = out_physical;
+  p.out_miss_host = out_miss_host;
+  p.out_miss_device = out_miss_device;
+  p.out_counts = out_counts;
+  p.head_columns = head_columns;
+  p.head_count = head_count;
+  p.head_width = head_width;
+  p.out_head_physical = out_head_physical;
+  p.workspace = static_cast<char *>(workspace);
+  p.status = device_status;
+  return hs::resolve_common(p, workspace_bytes, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int hs_resolve_rows_batched(int batch, const int32_t *positions, int64_t count,
+                                       const uint64_t *source_ptrs,
+                                       const uint64_t *resident_ptrs, int64_t table_pages,
+                                       const uint64_t *hot_ptrs, int64_t hot_blocks,
+                                       const uint64_t *tags_ptrs, const uint64_t *lru_ptrs,
+                                       int64_t hot_rows, const int32_t *lengths,
+                                       int page_size, int64_t *out_physical,
+                                       int64_t *out_miss_host, int64_t *out_miss_device,
+                                       int64_t *out_counts, void *workspace,
+                                       size_t workspace_bytes, int32_t *device_status,
+                                       hs_stream stream) {
+  if (!source_ptrs || !resident_ptrs || !hot_ptrs || !tags_ptrs || !lru_ptrs || !lengths)
+    return hs::set_error(HS_ERR_INVALID_ARGUMENT, "resolve: null pointer array or lengths");
+  hs::ResolveParams p{};
+  p.batch = batch;
+  p.positions = positions;
+  p.positions_i64 = 0;
+  p.count = count;
+  p.source = {nullptr, 0, source_ptrs};
+  p.resident = {nullptr, 0, resident_ptrs};
+  p.hot = {nullptr, 0, hot_ptrs};
+  p.tags = {nullptr, 0, tags_ptrs};
+  p.lru = {nullptr, 0, lru_ptrs};
+  p.table_pages = table_pages;
+  p.hot_blocks = hot_blocks;
+  p.hot_rows = hot_rows;
+  p.lengths = {lengths, 0};
+  p.page_size = page_size;
+  p.out_physical = out_physical;
+  p.out_miss_host = out_miss_host;
+  p.out_miss_device = out_miss_device;
+  p.out_counts = out_counts;
+  p.workspace = static_cast<char *>(workspace);
+  p.status = device_status;
+  return hs::resolve_common(p, workspace_bytes, static_cast<cudaStream_t>(stream));
+}

@@ -1,0 +1,62 @@
+"""Routes the reference package's hot path through libhisparse.
+
+``install(nano_hisparse)`` rebinds, inside an imported reference package, the
+names its decode path looks up at call time, so that the reference's own
+HybridKVCache, Model and Engine run Quest selection, the row resolver, the
+miss gather and row attention on the sm_100a kernels:
+
+  nano_hisparse.selection.quest_selection / model.quest_selection  (model.py:199-208)
+  nano_hisparse.hybrid.resolve_rows                                 (hybrid.py:431-440)
+  nano_hisparse.hybrid.LogicalTopK                                  (hybrid.py:406-409)
+  nano_hisparse.row_kernels.MappedHost / gather_rows / attend_rows  (hybrid.py:108-111,
+                                                                     447-451; attention.py:22-25)
+
+The reference's residency policy, storage, model and engine are untouched.
+``uninstall`` restores the original bindings.
+"""
+
+from __future__ import annotations
+
+import importlib
+
+from . import row_kernels as _rk
+from .row_index import LogicalTopK, resolve_rows
+from .selection import quest_selection
+
+_BINDINGS = [
+    ("selection", "quest_selection", quest_selection),
+    ("model", "quest_selection", quest_selection),
+    ("hybrid", "resolve_rows", resolve_rows),
+    ("hybrid", "LogicalTopK", LogicalTopK),
+    ("row_kernels", "MappedHost", _rk.MappedHost),
+    ("row_kernels", "gather_rows", _rk.gather_rows),
+    ("row_kernels", "attend_rows", _rk.attend_rows),
+]
+_saved: dict = {}
+
+
+def install(package) -> list[str]:
+    """Rebind the reference's hot-path names; returns the names rebound.
+
+    ``package`` is the imported reference package (``import nano_hisparse``).
+    The reference's row_kernels module imports Triton at import time, so the
+    reference must be importable as a whole (as on a CUDA host).
+    """
+    done = []
+    for module_name, attr, replacement in _BINDINGS:
+        module = importlib.import_module(f"{package.__name__}.{module_name}")
+        key = (package.__name__, module_name, attr)
+        if key not in _saved:
+            _saved[key] = getattr(module, attr)
+        setattr(module, attr, replacement)
+        done.append(f"{module_name}.{attr}")
+    return done
+
+
+def uninstall(package) -> None:
+    for (pkg, module_name, attr), original in list(_saved.items()):
+        if pkg != package.__name__:
+            continue
+        module = importlib.import_module(f"{pkg}.{module_name}")
+        setattr(module, attr, original)
+        del _saved[(pkg, module_name, attr)]

@@ -1,0 +1,493 @@
+"""Generates the golden fixtures under tests/golden/ by running the REFERENCE
+implementation (KiritoHugh/nano-hisparse, CPU torch path) on seeded inputs.
+
+This script is the only code that imports the reference; it runs where the
+reference tree is available and writes plain tensors, so the tests that read
+the fixtures need neither the reference nor a network:
+
+    python tests/golden/make_fixtures.py --reference /path/to/nano-hisparse
+
+Fixtures (torch.save of dicts of tensors / ints / lists, loaded with
+weights_only=True):
+  resolver_cases.pt   resolve_rows (row_index.py:62-140) on random tables,
+                      including the known-answer vector of
+                      tests/test_selection.py:36-50
+  quest_cases.pt      quest_selection (selection.py:69-91) on random
+                      queries/metadata, plus the known answers of
+                      tests/test_selection.py:18-33
+  attention_cases.pt  the torch path of row_attention (attention.py:26-35)
+                      on random pools and rows, shared and per-head
+  scenarios.pt        every resolve/gather/attention call made by
+                      HybridKVCache in scripted sessions that restate the
+                      reference's own cache tests (test_hybrid.py,
+                      test_residency.py) and trace replays (trace.py,
+                      test_trace.py), with the final row counters
+"""
+
+from __future__ import annotations
+
+import argparse
+import math
+import sys
+from pathlib import Path
+
+import numpy as np
+import torch
+
+OUT = Path(__file__).resolve().parent
+
+
+def load_reference(path):
+    sys.path.insert(0, str(path))
+    import nano_hisparse  # noqa: F401
+
+    return nano_hisparse
+
+
+# ---------------------------------------------------------------------------
+# resolver
+# ---------------------------------------------------------------------------
+def random_tables(rng, length, page_size, hot_rows, host_pages, pool_blocks,
+                  resident_fraction, tag_fraction, hit_positions=None):
+    n = math.ceil(length / page_size)
+    source = rng.choice(host_pages, size=n, replace=False).astype(np.int32)
+    # a few unmaterialised pages (source -1) exercise the "invalid" path
+    if n > 4:
+        source[rng.choice(n - 2, size=max(1, n // 50), replace=False)] = -1
+    hot_blocks = math.ceil(hot_rows / page_size)
+    blocks = rng.permutation(pool_blocks)
+    hot = blocks[:hot_blocks].astype(np.int32)
+    resident = np.full(n, -1, dtype=np.int32)
+    res_pages = rng.choice(n, size=int(n * resident_fraction), replace=False)
+    resident[res_pages] = blocks[hot_blocks:hot_blocks + len(res_pages)]
+    tags = np.full(hot_rows, -1, dtype=np.int32)
+    candidates = []
+    if hit_positions is not None:
+        for t in hit_positions:
+            if not 0 <= t < length:
+                continue
+            p = t // page_size
+            if source[p] >= 0 and resident[p] < 0:
+                candidates.append(int(source[p]) * page_size + t % page_size)
+    candidates = list(dict.fromkeys(candidates))
+    rng.shuffle(candidates)
+    n_tags = int(hot_rows * tag_fraction)
+    chosen = candidates[: n_tags // 2]
+    extra = rng.choice(host_pages * page_size, size=n_tags, replace=False)
+    for v in extra:
+        if len(chosen) >= n_tags:
+            break
+        if int(v) not in chosen:
+            chosen.append(int(v))
+    chosen = list(dict.fromkeys(chosen))[:n_tags]
+    slots = rng.choice(hot_rows, size=len(chosen), replace=False)
+    tags[slots] = chosen
+    lru = rng.permutation(hot_rows).astype(np.int64)
+    return source, resident, hot, tags, lru
+
+
+def resolver_cases(ref):
+    from nano_hisparse.row_index import LogicalTopK, resolve_rows
+
+    cases = []
+
+    def run(positions, source, resident, hot, tags, lru, length, page_size, name,
+            dtype=torch.int32):
+        t = {k: torch.tensor(v) for k, v in dict(source=source, resident=resident, hot=hot,
+                                                    tags=tags, lru=lru).items()}
+        before = {k: v.clone() for k, v in t.items()}
+        pos = torch.tensor(positions, dtype=dtype)
+        plan = resolve_rows(LogicalTopK(pos), t["source"], t["resident"], t["hot"], t["tags"],
+                            t["lru"], length, page_size)
+        cases.append({
+            "name": name, "positions": pos, **before, "length": length,
+            "page_size": page_size,
+            "physical": plan.physical_rows.clone(), "miss_host": plan.miss_host_rows.clone(),
+            "miss_device": plan.miss_device_rows.clone(), "counts": plan.counts.clone(),
+            "tags_after": t["tags"].clone(), "lru_after": t["lru"].clone(),
+        })
+
+    # known-answer vector: tests/test_selection.py:36-50 (int64 tables)
+    run([9, 2, 6, 9, 14, -1], np.array([5, 2, 9, 4]), np.array([-1, 7, -1, 3]),
+        np.array([6, 1]), np.array([-1, -1, -1, -1, -1, 22, -1, -1]),
+        np.array([0, 1, 2, 3, 4, 6, 7, 5]), 16, 4, "kat_test_selection", torch.int64)
+    rng = np.random.default_rng(1234)
+    shapes = [  # (K, H, P, length)
+        (4, 4, 4, 32), (6, 8, 4, 16), (16, 16, 3, 61), (32, 64, 7, 300), (64, 64, 16, 1000),
+        (100, 128, 4, 700), (256, 512, 16, 4096), (500, 512, 5, 3333), (1000, 2048, 16, 16384),
+        (2048, 4096, 16, 32768), (4096, 8192, 64, 131072),
+    ]
+    for ci, (k, h, p, length) in enumerate(shapes):
+        for variant in range(3):
+            n = math.ceil(length / p)
+            # positions: whole pages (Quest-like) with noise, duplicates and invalid ids
+            pages = rng.choice(n, size=max(1, k // p), replace=False)
+            pos = (pages[:, None] * p + np.arange(p)[None, :]).reshape(-1)
+            pos = pos[pos < length][:k]
+            if len(pos) < k:
+                pos = np.concatenate([pos, rng.integers(0, length, size=k - len(pos))])
+            pos = rng.permutation(pos)
+            m = max(1, k // 10)
+            idx = rng.choice(k, size=m, replace=False)
+            if variant >= 1:
+                pos[idx[: m // 3]] = -1
+                pos[idx[m // 3: 2 * m // 3]] = length + rng.integers(0, 5, size=len(idx[m // 3: 2 * m // 3]))
+                dup_src = rng.choice(k, size=len(idx[2 * m // 3:]))
+                pos[idx[2 * m // 3:]] = pos[dup_src]
+            if variant == 2:
+                pos = np.sort(pos)
+            tables = random_tables(rng, length, p, h, host_pages=max(4 * n, 64),
+                                   pool_blocks=math.ceil(h / p) + n + 8,
+                                   resident_fraction=[0.25, 0.1, 0.5][variant],
+                                   tag_fraction=[0.5, 1.0, 0.2][variant], hit_positions=pos)
+            run(pos.astype(np.int64), *tables, length, p, f"random_{ci}_{variant}")
+    return cases
+
+
+# ---------------------------------------------------------------------------
+# Quest
+# ---------------------------------------------------------------------------
+def page_bounds(keys, page_size, pages):
+    """min/max over the tokens of each page (storage.py:302-309 semantics)."""
+    t, hkv, d = keys.shape
+    mn = torch.full((pages, hkv, d), torch.inf, dtype=keys.dtype)
+    mx = torch.full((pages, hkv, d), -torch.inf, dtype=keys.dtype)
+    for p in range(pages):
+        chunk = keys[p * page_size:(p + 1) * page_size]
+        if len(chunk):
+            mn[p] = chunk.float().amin(0).to(keys.dtype)
+            mx[p] = chunk.float().amax(0).to(keys.dtype)
+    return mn, mx
+
+
+def quest_cases(ref):
+    from nano_hisparse.selection import quest_selection
+
+    cases = []
+    # known answers: tests/test_selection.py:18-33
+    low = torch.tensor([[[-10.0, 0.0]], [[1.0, 0.0]], [[0.0, 0.0]]])
+    high = torch.tensor([[[10.0, 0.0]], [[1.0, 0.0]], [[0.0, 0.0]]])
+    bounds = torch.tensor([[[9.0, 0.0]], [[0.0, 10.0]], [[-1.0, -1.0]]])
+    for name, q, mn, mx, length, p, top, sink in [
+        ("kat_mean_cancels", torch.tensor([[1.0, 0.0]]), low, high, 5, 2, 2, False),
+        ("kat_head_mean_first", torch.eye(2), bounds, bounds, 5, 2, 2, False),
+    ]:
+        sel = quest_selection(q, mn, mx, length, p, top, keep_sink=sink)
+        cases.append({"name": name, "query": q, "minimum": mn, "maximum": mx, "length": length,
+                      "page_size": p, "top_pages": top, f"tokens_{int(sink)}":
+                      list(sel.positions[0]), f"pages_{int(sink)}": sel.pages})
+    gen = torch.Generator().manual_seed(2024)
+    small = [  # (Hq, Hkv, D, P, length, top) — every dtype
+        (8, 2, 32, 16, 190, 4), (8, 2, 32, 16, 96, 4), (4, 2, 24, 7, 100, 5),
+        (6, 2, 24, 3, 50, 3), (2, 1, 8, 4, 33, 3), (4, 1, 80, 5, 203, 7),
+        (64, 8, 64, 4, 256, 10), (8, 2, 32, 16, 190, 1), (8, 2, 32, 16, 190, 20),
+    ]
+    large = [  # config-shaped heads/dims, bfloat16 only (size of the fixture)
+        (32, 8, 128, 16, 2048, 16), (32, 8, 128, 16, 2000, 100), (28, 4, 128, 64, 8192, 8),
+    ]
+    shapes = [(s, d) for s in small for d in (torch.float32, torch.bfloat16, torch.float16)]
+    shapes += [(s, torch.bfloat16) for s in large]
+    for ci, ((hq, hkv, d, p, length, top), dtype) in enumerate(shapes):
+        pages = math.ceil(length / p)
+        keys = torch.randn(length, hkv, d, generator=gen).to(dtype)
+        mn, mx = page_bounds(keys, p, pages + 3)  # spare (unused) table pages
+        q = torch.randn(hq, d, generator=gen).to(dtype)
+        case = {"name": f"random_{ci}_{str(dtype)[6:]}", "query": q, "minimum": mn,
+                "maximum": mx, "length": length, "page_size": p, "top_pages": top}
+        for sink in (True, False):
+            sel = quest_selection(q, mn, mx, length, p, top, keep_sink=sink)
+            case[f"tokens_{int(sink)}"] = list(sel.positions[0])
+            case[f"pages_{int(sink)}"] = sel.pages
+        cases.append(case)
+    return cases
+
+
+# ---------------------------------------------------------------------------
+# attention
+# ---------------------------------------------------------------------------
+class _Lease:
+    def __init__(self, rows):
+        self.plan = type("Plan", (), {"physical_rows": rows})()
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *_):
+        return False
+
+
+class _RowsOnlyCache:
+    """Duck-typed cache whose resolve() yields given physical rows; lets the
+    reference's own torch attention path (attention.py:26-35) run on a pool."""
+
+    def __init__(self, config, pool, rows):
+        self.config, self.pool, self.rows = config, pool, rows
+        self.storage = type("S", (), {"cuda": False})()
+
+    def resolve(self, request_id, layer, topk):
+        return _Lease(self.rows)
+
+
+def attention_cases(ref):
+    from nano_hisparse.attention import row_attention
+    from nano_hisparse.config import CacheConfig
+    from nano_hisparse.row_index import LogicalTopK
+
+    gen = torch.Generator().manual_seed(77)
+    cases = []
+    shapes = [  # (Hq, Hkv, D, P, blocks, K, per_head, dtypes)
+        (2, 1, 8, 4, 3, 4, False, 3), (4, 2, 8, 3, 8, 5, False, 3), (6, 2, 24, 7, 6, 4, False, 3),
+        (4, 2, 8, 3, 8, 3, True, 3), (8, 2, 32, 16, 24, 64, False, 3),
+        (4, 1, 80, 5, 9, 17, True, 3), (3, 3, 16, 2, 5, 6, False, 3),
+        (32, 8, 128, 16, 12, 150, False, 1), (28, 4, 128, 64, 3, 150, False, 1),
+    ]
+    all_dtypes = (torch.bfloat16, torch.float32, torch.float16)
+    for ci, (hq, hkv, d, p, blocks, k, per_head, nd) in enumerate(shapes):
+        for dtype in all_dtypes[:nd]:
+            config = CacheConfig(gpu_pages=blocks, host_pages=4, page_size=p, kv_heads=hkv,
+                                 head_dim=d, device="cpu", dtype=dtype)
+            pool = torch.randn(blocks, 2, p, hkv, d, generator=gen).to(dtype)
+            q = torch.randn(hq, d, generator=gen).to(dtype)
+            rows_total = blocks * p
+            if per_head:
+                rows = torch.stack([torch.randperm(rows_total, generator=gen)[:k] for _ in range(hq)])
+                rows[torch.rand(hq, k, generator=gen) < 0.2] = -1
+            else:
+                rows = torch.randperm(rows_total, generator=gen)[:k].clone()
+                rows[torch.rand(k, generator=gen) < 0.15] = -1
+            cache = _RowsOnlyCache(config, pool, rows)
+            topk = LogicalTopK(torch.zeros(1, dtype=torch.int32),
+                               torch.zeros(hq, 1, dtype=torch.int64) if per_head else None)
+            out = row_attention(q, cache, "r", 0, topk, backend="torch")
+            cases.append({"name": f"attn_{ci}_{str(dtype)[6:]}", "query": q, "pool": pool,
+                          "rows": rows, "page_size": p, "out": out})
+    # all rows invalid -> zeros (tests/test_hybrid.py:267-274)
+    config = CacheConfig(gpu_pages=3, host_pages=4, page_size=4, kv_heads=1, head_dim=8,
+                         device="cpu")
+    pool = torch.randn(3, 2, 4, 1, 8, generator=gen)
+    q = torch.randn(2, 8, generator=gen)
+    rows = torch.full((4,), -1, dtype=torch.int64)
+    out = row_attention(q, _RowsOnlyCache(config, pool, rows), "r", 0,
+                        LogicalTopK(torch.zeros(1, dtype=torch.int32)), backend="torch")
+    cases.append({"name": "attn_all_invalid", "query": q, "pool": pool, "rows": rows,
+                  "page_size": 4, "out": out})
+    return cases
+
+
+# ---------------------------------------------------------------------------
+# cache scenarios (recorded at the resolve / gather / attention boundary)
+# ---------------------------------------------------------------------------
+class Recorder:
+    def __init__(self, ref):
+        import nano_hisparse.attention as attention_mod
+        import nano_hisparse.hybrid as hybrid_mod
+
+        self.records, self.current = [], {}
+        self.hybrid_mod, self.attention_mod = hybrid_mod, attention_mod
+        self.orig_resolve_rows = hybrid_mod.resolve_rows
+        self.orig_cache_resolve = hybrid_mod.HybridKVCache.resolve
+        self.orig_row_attention = attention_mod.row_attention
+        rec = self
+
+        def resolve_rows(topk, source, resident, hot, tags, lru, length, page_size):
+            before = {"positions": topk.positions.clone(),
+                      "head_columns": None if topk.head_columns is None
+                      else topk.head_columns.clone(),
+                      "source": source.clone(), "resident": resident.clone(),
+                      "hot": hot.clone(), "tags": tags.clone(), "lru": lru.clone(),
+                      "length": int(length), "page_size": int(page_size)}
+            plan = rec.orig_resolve_rows(topk, source, resident, hot, tags, lru, length,
+                                         page_size)
+            rec.current.update(before)
+            rec.current.update({"physical": plan.physical_rows.clone(),
+                                "miss_host": plan.miss_host_rows.clone(),
+                                "miss_device": plan.miss_device_rows.clone(),
+                                "counts": plan.counts.clone(), "tags_after": tags.clone(),
+                                "lru_after": lru.clone()})
+            return plan
+
+        def cache_resolve(cache, request_id, layer, topk):
+            rec.current["pool_before"] = cache.pool.clone()
+            host = cache.storage.host
+            lease = rec.orig_cache_resolve(cache, request_id, layer, topk)
+            rec.current["pool_after"] = cache.pool.clone()
+            used = sorted({int(h) // cache.config.page_size
+                           for h in lease.plan.miss_host_rows.tolist() if h >= 0})
+            rec.current["host_blocks"] = torch.tensor(used, dtype=torch.int64)
+            rec.current["host_data"] = host[used].clone() if used else host[:0].clone()
+            rec.current["host_pages"] = int(host.shape[0])
+            return lease
+
+        def row_attention(query, cache, request_id, layer, topk, backend="auto"):
+            rec.current = {}
+            out = rec.orig_row_attention(query, cache, request_id, layer, topk, backend)
+            if "physical" in rec.current:
+                rec.current.update({"query": query.clone(), "out": out.clone()})
+                rec.records.append(rec.current)
+            rec.current = {}
+            return out
+
+        hybrid_mod.resolve_rows = resolve_rows
+        hybrid_mod.HybridKVCache.resolve = cache_resolve
+        attention_mod.row_attention = row_attention
+        self.row_attention = row_attention
+
+    def take(self):
+        records, self.records = self.records, []
+        return records
+
+    def restore(self):
+        self.hybrid_mod.resolve_rows = self.orig_resolve_rows
+        self.hybrid_mod.HybridKVCache.resolve = self.orig_cache_resolve
+        self.attention_mod.row_attention = self.orig_row_attention
+
+
+def scenarios(ref):
+    from dataclasses import replace
+
+    from nano_hisparse.config import CacheConfig
+    from nano_hisparse.hybrid import HotConfig, HybridKVCache
+    from nano_hisparse.row_index import LogicalTopK
+    from nano_hisparse.selection import Selection
+    from nano_hisparse.trace import replay_trace, synthetic_trace
+
+    rec = Recorder(ref)
+    out = []
+    torch.set_num_threads(1)
+
+    def make(**overrides):
+        config = replace(CacheConfig(gpu_pages=3, host_pages=64, page_size=4, kv_heads=1,
+                                     head_dim=8, device="cpu"), **overrides)
+        return HybridKVCache(config, HotConfig(4, 4))
+
+    def write(cache, name="a", length=32, layer=0):
+        k, v = [torch.randn(length, cache.config.kv_heads, cache.config.head_dim,
+                            dtype=cache.config.dtype) for _ in range(2)]
+        cache.write(name, layer, k, v)
+        return k, v
+
+    def topk(values):
+        return LogicalTopK(torch.tensor(values, dtype=torch.int32))
+
+    def finish(name, cache, **extra):
+        out.append({"name": name, "records": rec.take(),
+                    "row_stats": cache.snapshot()["row_stats"], **extra})
+
+    # test_hybrid.py:42-62 — resident hits bypass the hot buffer; counters
+    torch.manual_seed(101)
+    cache = make()
+    cache.reserve("a", 40, 1)
+    write(cache)
+    q = torch.randn(2, 8)
+    for _ in range(2):
+        rec.row_attention(q, cache, "a", 0, topk([0, 7, 17, 31]))
+    finish("row_misses_and_resident_hits", cache)
+
+    # test_hybrid.py:76-93 — late hits are protected; duplicates and -1
+    torch.manual_seed(102)
+    cache = make()
+    cache.reserve("a", 40, 1)
+    write(cache)
+    q = torch.randn(2, 8)
+    for selected in ([0, 4, 8, 12], [16, 4, 8, 12], [4, 4, -1, 12]):
+        rec.row_attention(q, cache, "a", 0, topk(selected))
+    finish("late_hits_protected", cache)
+
+    # test_hybrid.py:96-121 — shared and legacy per-head masks, fragmented hot blocks
+    for shared in (True, False):
+        torch.manual_seed(103)
+        config = CacheConfig(gpu_pages=8, host_pages=64, page_size=3, kv_heads=2, head_dim=8,
+                             device="cpu")
+        cache = HybridKVCache(config, HotConfig(6, 6, transition_watermark=0))
+        cache.reserve("a", 40, 1)
+        cache.reserve("b", 40, 1)
+        for _ in range(3):
+            write(cache, "a", 3)
+            write(cache, "b", 3)
+        write(cache, "b", 3)
+        cache.storage.synchronize()
+        cache.transition_to_host("a", 0)
+        write(cache, "a", 18)
+        q = torch.randn(4, 8)
+        positions = [0, 2, 7, 11, 19] if shared else [[0, 7], [2], [7, 11], [19, 0]]
+        cache.attention(q, "a", 0, selection=Selection.from_tokens(positions, 27, 3, 4))
+        finish(f"masks_{'shared' if shared else 'legacy'}", cache)
+
+    # test_hybrid.py:247-264 — randomized requests/layers with appends
+    torch.manual_seed(17)
+    cache = make(gpu_pages=12, host_pages=256)
+    for name in ("a", "b"):
+        cache.reserve(name, 64, 2)
+        for layer in range(2):
+            write(cache, name, 19, layer)
+    lengths = {("a", 0): 19, ("a", 1): 19, ("b", 0): 19, ("b", 1): 19}
+    for step in range(32):
+        name, layer = ("a", "b")[step % 2], (step // 2) % 2
+        write(cache, name, 1, layer)
+        lengths[name, layer] += 1
+        n = lengths[name, layer]
+        selected = [*torch.randperm(n - 1)[:3].tolist(), n - 1]
+        q = torch.randn(2, 8)
+        rec.row_attention(q, cache, name, layer, topk(selected))
+    finish("randomized_requests_layers", cache)
+
+    # test_hybrid.py:267-274 — invalid / padding-only top-k
+    torch.manual_seed(104)
+    cache = make()
+    cache.reserve("a", 40, 1)
+    write(cache)
+    rec.row_attention(torch.randn(2, 8), cache, "a", 0, topk([-1, -2, 100, 32]))
+    finish("invalid_padding_only", cache)
+
+    # test_residency.py:174-199 — H = U, every selected row misses
+    torch.manual_seed(29)
+    cache = HybridKVCache(CacheConfig(gpu_pages=3, host_pages=128, page_size=4, kv_heads=1,
+                                      head_dim=8, device="cpu"),
+                          HotConfig(4, 4, transition_watermark=None))
+    cache.reserve("a", 64, 1)
+    write(cache, "a", 32)
+    cache.reset_stats()
+    choices = ([0, 4, 8, 12], [1, 5, 9, 13])
+    for step in range(16):
+        write(cache, "a", 1)
+        rec.row_attention(torch.randn(2, 8), cache, "a", 0, topk(choices[step % 2]))
+    finish("all_miss_minimum_hot", cache)
+
+    # low precision, odd shapes (test_hybrid.py:177-189, run on the CPU path)
+    for dtype in (torch.float16, torch.bfloat16):
+        torch.manual_seed(105)
+        cache = make(dtype=dtype, page_size=7, head_dim=24, kv_heads=2)
+        cache.reserve("a", 100, 1)
+        write(cache, length=80)
+        q = torch.randn(6, 24).to(dtype)
+        rec.row_attention(q, cache, "a", 0, topk([0, 13, 39, 79]))
+        finish(f"low_precision_{str(dtype)[6:]}", cache)
+
+    # trace replays: test_trace.py:18-56 / README locality table
+    for pattern, capacity in [("reuse", 4), ("alternating", 4), ("alternating", 8),
+                              ("streaming", 8), ("packed", 4)]:
+        report = replay_trace(synthetic_trace(pattern), capacity, "cpu")
+        out.append({"name": f"trace_{pattern}_{capacity}", "records": rec.take(),
+                    "row_stats": {k: report["summary"][k] for k in
+                                  ("resident_hits", "hot_hits", "misses", "h2d_bytes")},
+                    "hot_slots": [e["hot_slots"] for e in report["events"]]})
+    rec.restore()
+    return out
+
+
+def main():
+    parser = argparse.ArgumentParser(description=__doc__.split("\n\n")[0])
+    parser.add_argument("--reference", default="/root/reference")
+    args = parser.parse_args()
+    ref = load_reference(args.reference)
+    torch.set_num_threads(4)
+    for name, fn in [("resolver_cases", resolver_cases), ("quest_cases", quest_cases),
+                     ("attention_cases", attention_cases), ("scenarios", scenarios)]:
+        data = fn(ref)
+        path = OUT / f"{name}.pt"
+        torch.save(data, path)
+        print(f"{path.name}: {len(data)} cases, {path.stat().st_size / 1024:.0f} KiB")
+
+
+if __name__ == "__main__":
+    main()
