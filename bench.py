@@ -43,7 +43,9 @@ DTYPE = torch.bfloat16
 
 
 def workload_config():
+    reduced = REQUESTS != 16 or LAYERS != 32
     return {
+        **({"reduced_for_profiling": True} if reduced else {}),
         "workload": "config 2: Llama-3-8B-shaped sparse decode hot path (Quest select, row "
                     "resolve, host->pool miss gather, row attention) for every layer",
         "requests_per_gpu": REQUESTS, "layers": LAYERS, "context": CONTEXT,
@@ -403,13 +405,19 @@ def cpu_sample(seed=1, budget_s=10.0, threads=None, log=print):
 
 
 def main():
+    global REQUESTS, LAYERS
     parser = argparse.ArgumentParser(description=__doc__.split("\n\n")[0])
     parser.add_argument("--gpus", type=int, default=1)
     parser.add_argument("--steps", type=int, default=10)
     parser.add_argument("--warmup", type=int, default=3)
     parser.add_argument("--impl", default="hisparse_b200", choices=["hisparse_b200", "reference"])
     parser.add_argument("--no-cpu-baseline", action="store_true")
+    # Smaller request/layer counts are for ncu captures only; the bench line of
+    # configuration 2 uses the defaults.
+    parser.add_argument("--requests", type=int, default=REQUESTS)
+    parser.add_argument("--layers", type=int, default=LAYERS)
     args = parser.parse_args()
+    REQUESTS, LAYERS = args.requests, args.layers
     rank = int(os.environ.get("RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", 1))
     local_rank = int(os.environ.get("LOCAL_RANK", 0))

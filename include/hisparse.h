@@ -72,7 +72,9 @@ enum hs_device_flag {
   HS_DEV_ROW_OUT_OF_RANGE = 1,   /* a physical/host row beyond its buffer was skipped */
   HS_DEV_PAGES_EXCEED_TABLE = 2, /* ceil(length / page_size) exceeded the table capacity */
   HS_DEV_LRU_CORRUPT = 4,        /* an LRU entry outside [0, hot_rows) was skipped */
-  HS_DEV_MISSES_EXCEED_HOT = 8   /* more misses than hot rows: tags/lru left unchanged */
+  HS_DEV_MISSES_EXCEED_HOT = 8,  /* more misses than hot rows: tags/lru left unchanged */
+  HS_DEV_WAIT_TIMEOUT = 16,      /* a bounded wait for an async copy ran out (results invalid) */
+  HS_DEV_MISALIGNED = 32         /* a batched metadata pointer was not 16-byte aligned: skipped */
 };
 
 typedef void *hs_stream; /* cudaStream_t */
@@ -118,6 +120,10 @@ HS_API int hs_host_device_pointer(const void *host, void **device_alias);
  * The head sums are combined the same way (lane j adds heads j, j+32, ...
  * left to right, then the same xor tree) and divided by q_heads.
  */
+/* Workspace: per-request scores plus one completion counter per request. It
+ * must be zero-filled before its first use; every call leaves it zero-filled,
+ * so one workspace serves consecutive calls on one stream (calls that overlap
+ * on the GPU need separate workspaces). */
 HS_API size_t hs_quest_workspace_bytes(int batch, int64_t max_pages);
 
 HS_API int hs_quest_select(const void *query, int query_dtype, const void *minimum,
@@ -130,8 +136,10 @@ HS_API int hs_quest_select(const void *query, int query_dtype, const void *minim
 /* Batched over `batch` requests of one layer. query is [batch, q_heads,
  * head_dim] with `query_batch_stride` elements between requests;
  * minimum_ptrs/maximum_ptrs are device arrays of `batch` pointers to each
- * request's [>= max_pages, kv_heads, head_dim] metadata; lengths is a device
- * int32[batch]. out_tokens is [batch, out_capacity], out_counts int32[batch]. */
+ * request's [>= max_pages, kv_heads, head_dim] metadata, each 16-byte aligned
+ * (bulk copies read them; a misaligned request raises HS_DEV_MISALIGNED and
+ * is skipped); lengths is a device int32[batch]. out_tokens is
+ * [batch, out_capacity], out_counts int32[batch]. */
 HS_API int hs_quest_select_batched(int batch, const void *query, int64_t query_batch_stride,
                             int query_dtype, const uint64_t *minimum_ptrs,
                             const uint64_t *maximum_ptrs, int kv_dtype,

@@ -9,6 +9,8 @@
 // Softmax and accumulation are fp32.
 #include <math.h>
 
+#include <type_traits>
+
 #include "common.cuh"
 
 namespace hs {
@@ -32,6 +34,7 @@ struct AttendParams {
   int64_t out_batch_stride;
   int q_heads, kv_heads, head_dim, page_size;
   int splits, head_chunks;  // grid.y = kv_heads * head_chunks (shared) or q_heads (per head)
+  int page_shift;           // log2(page_size) when a power of two, else -1
   float scale;
   float *partials;  // [batch, q_heads, splits, head_dim + 2]
   int32_t *status;
@@ -180,6 +183,287 @@ __global__ void __launch_bounds__(kAttendThreads) attend_split_kernel(AttendPara
   }
 }
 
+// ---- tensor-core path: bf16 query and KV, head_dim 128, shared rows ------------
+//
+// One CTA of 8 warps serves one request over one split of the rows and every
+// KV head: rows arrive through a 3-stage cp.async pipeline as whole token rows
+// (K and V of all KV heads: contiguous 2 KiB runs for 8 heads, so DRAM pages
+// are read once), with 16-byte chunks XOR-swizzled by row so the ldmatrix
+// reads below are conflict-free. Warp w owns one (KV head, up to 16 query
+// heads) item and walks the stage in sub-tiles of 16 rows:
+//   S = Q K^T   m16n8k16 bf16 MMA, M = query heads (zero padded to 16),
+//               N = 8 rows, K = 16 head-dim elements; Q fragments stay in
+//               registers for the whole split;
+//   online softmax per head in fp32 (exp2 with log2(e) folded into the scale);
+//   O += P V    the S accumulators, rounded to bf16, are the A fragments of the
+//               second MMA; V fragments come from ldmatrix.trans.
+// Each warp writes one (max, sum, O) partial per (request, head, split) for
+// attend_merge_kernel.
+constexpr int kMmaThreads = 256;
+constexpr int kMmaWarps = kMmaThreads / 32;
+constexpr int kStages = 3;
+constexpr int kHeadBytes = 256;               // 128 bf16 of one KV head
+constexpr int kStageTarget = 64 * 1024;       // bytes of K+V per stage
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+  return (uint32_t)__cvta_generic_to_shared(p);
+}
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void *src, bool valid) {
+  const int bytes = valid ? 16 : 0;  // 0: zero-fill, nothing is read
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(dst), "l"(src),
+               "r"(bytes));
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n"); }
+template <int N> __device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;\n" ::"n"(N));
+}
+
+__device__ __forceinline__ void ldmatrix_x4(uint32_t addr, uint32_t &r0, uint32_t &r1,
+                                            uint32_t &r2, uint32_t &r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];\n"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldmatrix_x4_trans(uint32_t addr, uint32_t &r0, uint32_t &r1,
+                                                  uint32_t &r2, uint32_t &r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];\n"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+
+__device__ __forceinline__ void mma_bf16(float (&c)[4], const uint32_t (&a)[4], uint32_t b0,
+                                         uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, "
+      "{%4, %5, %6, %7}, {%8, %9}, {%0, %1, %2, %3};\n"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
+  const __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t *>(&v);
+}
+
+struct MmaShape {
+  int row_bytes;   // kv_heads * 256
+  int stage_rows;  // multiple of 16
+  int stage_bytes; // 2 * stage_rows * row_bytes
+};
+
+__host__ __device__ inline MmaShape mma_shape(int kv_heads) {
+  MmaShape m;
+  m.row_bytes = kv_heads * kHeadBytes;
+  int rows = kStageTarget / (2 * m.row_bytes);
+  rows = rows < 16 ? 16 : (rows / 16) * 16;
+  m.stage_rows = rows;
+  m.stage_bytes = 2 * rows * m.row_bytes;
+  return m;
+}
+
+// byte offset of 16-byte chunk `c` of stage row `r` (XOR swizzle by row)
+__device__ __forceinline__ uint32_t swz(int r, int c, int row_bytes) {
+  return (uint32_t)(r * row_bytes + ((c ^ (r & 7)) << 4));
+}
+
+__global__ void __launch_bounds__(kMmaThreads, 1) attend_mma_kernel(AttendParams p) {
+  extern __shared__ __align__(128) char smem[];
+  __shared__ int8_t row_ok[kStages][128];
+  const int split = blockIdx.x, b = blockIdx.z;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const MmaShape sh = mma_shape(p.kv_heads);
+  const int groups = p.q_heads / p.kv_heads;
+  const int items = p.kv_heads * p.head_chunks;
+  const bool active = warp < items;
+  const int kh = active ? warp / p.head_chunks : 0;
+  const int h0 = kh * groups + (warp % p.head_chunks) * 16;
+  const int hn = active ? min(16, kh * groups + groups - h0) : 0;
+  const int64_t chunk = ceil_div(p.count, p.splits);
+  const int64_t begin = split * chunk, end = min(p.count, begin + chunk);
+  const int64_t *rows = p.rows + (int64_t)b * p.rows_batch_stride;
+  const int64_t row_elems = (int64_t)p.kv_heads * 128;
+  const int64_t plane = (int64_t)p.page_size * row_elems;
+  const __nv_bfloat16 *pool = reinterpret_cast<const __nv_bfloat16 *>(p.pool);
+  const int tiles = begin < end ? (int)ceil_div(end - begin, sh.stage_rows) : 0;
+  const int chunks_per_row = sh.row_bytes / 16;
+
+  // Q fragments for the 8 k-steps: a0/a2 head lane/4, a1/a3 head lane/4 + 8
+  uint32_t qf[8][4];
+  {
+    const __nv_bfloat16 *qb =
+        static_cast<const __nv_bfloat16 *>(p.query) + (int64_t)b * p.query_batch_stride;
+    const int m0 = lane >> 2, kq = (lane & 3) * 2;
+#pragma unroll
+    for (int kk = 0; kk < 8; ++kk) {
+#pragma unroll
+      for (int part = 0; part < 4; ++part) {
+        const int m = m0 + ((part & 1) ? 8 : 0);
+        const int d = kk * 16 + kq + ((part & 2) ? 8 : 0);
+        uint32_t v = 0;
+        if (m < hn) v = *reinterpret_cast<const uint32_t *>(qb + (int64_t)(h0 + m) * 128 + d);
+        qf[kk][part] = v;
+      }
+    }
+  }
+
+  // loader: warp w copies rows w, w+8, ... of a stage; its lanes copy
+  // consecutive 16-byte chunks of the row (K and V of every KV head), so the
+  // row's address is computed once per warp
+  const int rows_per_warp = sh.stage_rows / kMmaWarps;
+  const int lane_chunks = (chunks_per_row + 31) / 32;
+  auto load_tile = [&](int t, int stage) {
+    char *kbase = smem + stage * sh.stage_bytes;
+    char *vbase = kbase + sh.stage_rows * sh.row_bytes;
+    for (int k = 0; k < rows_per_warp; ++k) {
+      const int r = warp + k * kMmaWarps;
+      const int64_t i = begin + (int64_t)t * sh.stage_rows + r;
+      const int64_t row = i < end ? rows[i] : -1;
+      int64_t blk = 0, off = 0;
+      if (row >= 0) {
+        if (p.page_shift >= 0) {
+          blk = row >> p.page_shift;
+          off = row & (p.page_size - 1);
+        } else {
+          blk = row / p.page_size;
+          off = row % p.page_size;
+        }
+      }
+      bool ok = row >= 0;
+      if (ok && blk >= p.pool_blocks) {
+        if (lane == 0) flag(p.status, HS_DEV_ROW_OUT_OF_RANGE);
+        ok = false;
+      }
+      const __nv_bfloat16 *src = ok ? pool + (blk * 2 * p.page_size + off) * row_elems : pool;
+      for (int u = 0; u < lane_chunks; ++u) {
+        const int c = u * 32 + lane;
+        if (c < chunks_per_row) {
+          cp_async16(smem_u32(kbase + swz(r, c, sh.row_bytes)), ok ? src + c * 8 : pool, ok);
+          cp_async16(smem_u32(vbase + swz(r, c, sh.row_bytes)), ok ? src + plane + c * 8 : pool,
+                     ok);
+        }
+      }
+      if (lane == 0) row_ok[stage][r] = ok;
+    }
+  };
+
+  constexpr float kLog2e = 1.4426950408889634f;
+  const float scale = p.scale * kLog2e;
+  float m_run[2] = {-INFINITY, -INFINITY};  // heads lane/4 and lane/4 + 8
+  float l_run[2] = {0.f, 0.f};
+  float o[16][4];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+
+#pragma unroll
+  for (int s = 0; s < kStages - 1; ++s) {
+    if (s < tiles) load_tile(s, s);
+    cp_async_commit();
+  }
+  for (int t = 0; t < tiles; ++t) {
+    if (t + kStages - 1 < tiles) load_tile(t + kStages - 1, (t + kStages - 1) % kStages);
+    cp_async_commit();
+    cp_async_wait<kStages - 1>();
+    __syncthreads();
+    const int stage = t % kStages;
+    const char *kbase = smem + stage * sh.stage_bytes;
+    const char *vbase = kbase + sh.stage_rows * sh.row_bytes;
+    for (int r0 = 0; active && r0 < sh.stage_rows; r0 += 16) {
+      // ---- S = Q K^T for 16 rows (two n-tiles of 8 rows) ----
+      float sacc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+      {
+        const int mi = lane >> 3, rr = lane & 7;
+        const int row = r0 + (mi >> 1) * 8 + rr;
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          uint32_t b0, b1, b2, b3;
+          ldmatrix_x4(smem_u32(kbase + swz(row, kh * 16 + 2 * kk + (mi & 1), sh.row_bytes)),
+                      b0, b1, b2, b3);
+          mma_bf16(sacc[0], qf[kk], b0, b1);
+          mma_bf16(sacc[1], qf[kk], b2, b3);
+        }
+      }
+      // ---- online softmax (per head; a quad of lanes shares a head) ----
+      float pr[2][4];
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh) {
+        float mx = -INFINITY;
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const int r = r0 + nt * 8 + (lane & 3) * 2 + e;
+            float v = sacc[nt][hh * 2 + e] * scale;
+            v = row_ok[stage][r] ? v : -INFINITY;
+            sacc[nt][hh * 2 + e] = v;
+            mx = fmaxf(mx, v);
+          }
+        mx = fmaxf(mx, __shfl_xor_sync(kFullMask, mx, 1));
+        mx = fmaxf(mx, __shfl_xor_sync(kFullMask, mx, 2));
+        const float m_new = fmaxf(m_run[hh], mx);
+        const float alpha = m_run[hh] == -INFINITY ? 0.f : exp2f(m_run[hh] - m_new);
+        float sum = 0.f;
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const float v = sacc[nt][hh * 2 + e];
+            const float w = v == -INFINITY ? 0.f : exp2f(v - m_new);
+            pr[nt][hh * 2 + e] = w;
+            sum += w;
+          }
+        l_run[hh] = l_run[hh] * alpha + sum;
+        m_run[hh] = m_new;
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          o[i][hh * 2] *= alpha;
+          o[i][hh * 2 + 1] *= alpha;
+        }
+      }
+      // ---- O += P V ----
+      uint32_t pa[4] = {pack_bf16(pr[0][0], pr[0][1]), pack_bf16(pr[0][2], pr[0][3]),
+                        pack_bf16(pr[1][0], pr[1][1]), pack_bf16(pr[1][2], pr[1][3])};
+      {
+        const int mi = lane >> 3, rr = lane & 7;
+        const int row = r0 + (mi & 1) * 8 + rr;
+#pragma unroll
+        for (int dn = 0; dn < 16; dn += 2) {
+          uint32_t b0, b1, b2, b3;
+          ldmatrix_x4_trans(
+              smem_u32(vbase + swz(row, kh * 16 + dn + (mi >> 1), sh.row_bytes)), b0, b1, b2, b3);
+          mma_bf16(o[dn], pa, b0, b1);
+          mma_bf16(o[dn + 1], pa, b2, b3);
+        }
+      }
+    }
+    __syncthreads();
+  }
+  cp_async_wait<0>();
+  if (!active) return;
+
+  // ---- one (max, sum, O) partial per head of this warp ----
+  const int stride = 128 + 2;
+#pragma unroll
+  for (int hh = 0; hh < 2; ++hh) {
+    float l = l_run[hh];
+    l += __shfl_xor_sync(kFullMask, l, 1);
+    l += __shfl_xor_sync(kFullMask, l, 2);
+    const int m = (lane >> 2) + hh * 8;
+    if (m >= hn) continue;
+    float *dst = p.partials + (((int64_t)b * p.q_heads + h0 + m) * p.splits + split) * stride;
+    if ((lane & 3) == 0) {
+      dst[128] = m_run[hh] * 0.6931471805599453f;  // log2 units -> natural log for the merge
+      dst[129] = l;
+    }
+#pragma unroll
+    for (int dn = 0; dn < 16; ++dn) {
+      const int d = dn * 8 + (lane & 3) * 2;
+      dst[d] = o[dn][hh * 2];
+      dst[d + 1] = o[dn][hh * 2 + 1];
+    }
+  }
+}
+
 template <typename TQ>
 __global__ void attend_merge_kernel(AttendParams p) {
   const int h = blockIdx.x, b = blockIdx.y;
@@ -203,11 +487,47 @@ __global__ void attend_merge_kernel(AttendParams p) {
   }
 }
 
+__host__ inline int mma_splits(int batch, int64_t count, int stage_rows, int sms) {
+  int64_t s = sms / batch;
+  const int64_t by_rows = ceil_div(count, 2 * stage_rows);
+  if (s > by_rows) s = by_rows;
+  if (s > kMaxSplits) s = kMaxSplits;
+  if (s < 1) s = 1;
+  return (int)s;
+}
+
+// Upper bound of the splits either attention path uses (workspace sizing).
+__host__ inline int max_splits(int batch, int kv_heads, int64_t count, int sms) {
+  const int a = attend_splits(batch, kv_heads, count, sms);
+  const int m = mma_splits(batch, count, mma_shape(kv_heads).stage_rows, sms);
+  return a > m ? a : m;
+}
+
 template <typename TQ, typename TKV>
 int launch(AttendParams &p, cudaStream_t stream) {
+  const int groups = p.q_heads / p.kv_heads;
+  if constexpr (std::is_same<TQ, __nv_bfloat16>::value && std::is_same<TKV, __nv_bfloat16>::value) {
+    const int chunks16 = (groups + 15) / 16;
+    if (p.head_dim == 128 && p.rows_head_stride == 0 && p.kv_heads * chunks16 <= kMmaWarps &&
+        (reinterpret_cast<uintptr_t>(p.pool) & 15) == 0) {
+      p.head_chunks = chunks16;
+      const MmaShape sh = mma_shape(p.kv_heads);
+      const int kMmaSmem = kStages * sh.stage_bytes;
+      p.splits = mma_splits(p.batch, p.count, sh.stage_rows, sm_count());
+      if (cudaFuncSetAttribute(attend_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               kMmaSmem) != cudaSuccess)
+        return set_error(HS_ERR_CUDA, "attend: cannot reserve %d bytes of shared memory",
+                         kMmaSmem);
+      dim3 grid(p.splits, 1, p.batch);
+      attend_mma_kernel<<<grid, kMmaThreads, kMmaSmem, stream>>>(p);
+      int rc = check_launch("attend_mma_kernel");
+      if (rc != HS_OK) return rc;
+      attend_merge_kernel<TQ><<<dim3(p.q_heads, p.batch), 128, 0, stream>>>(p);
+      return check_launch("attend_merge_kernel");
+    }
+  }
   const int C = (p.head_dim + 31) / 32;
   const int Cp = C <= 1 ? 1 : C <= 2 ? 2 : C <= 4 ? 4 : 8;
-  const int groups = p.q_heads / p.kv_heads;
   p.head_chunks = (groups + kMaxGroup - 1) / kMaxGroup;
   const bool shared_rows = p.rows_head_stride == 0;
   dim3 grid(p.splits, shared_rows ? p.kv_heads * p.head_chunks : p.q_heads, p.batch);
@@ -238,7 +558,7 @@ template <typename TQ> int dispatch_kv(int kv_dtype, AttendParams &p, cudaStream
 extern "C" size_t hs_attend_workspace_bytes(int batch, int q_heads, int kv_heads,
                                             int head_dim, int64_t count) {
   if (batch < 1 || q_heads < 1 || kv_heads < 1 || head_dim < 1 || count < 1) return 0;
-  const int splits = hs::attend_splits(batch, kv_heads, count, hs::sm_count());
+  const int splits = hs::max_splits(batch, kv_heads, count, hs::sm_count());
   return (size_t)batch * q_heads * splits * (head_dim + 2) * sizeof(float);
 }
 
@@ -282,6 +602,10 @@ extern "C" int hs_attend_rows(int batch, const void *query, int64_t query_batch_
   p.page_size = page_size;
   p.splits = attend_splits(batch, kv_heads, count, sm_count());
   p.scale = (float)(1.0 / sqrt((double)head_dim));
+  p.page_shift = -1;
+  if ((page_size & (page_size - 1)) == 0)
+    for (int sh = 0; sh < 31; ++sh)
+      if ((1 << sh) == page_size) p.page_shift = sh;
   p.partials = static_cast<float *>(workspace);
   p.status = device_status;
   cudaStream_t s = static_cast<cudaStream_t>(stream);

@@ -1,18 +1,29 @@
 // (1) Quest page selection: page scoring over the K min/max metadata, shared
-// top-k with forced sink/tail pages and page->token expansion.
+// top-k with forced sink/tail pages and page->token expansion, in one launch.
 //
 // Reference: nano_hisparse/selection.py:69-91 (quest_selection),
 // selection.py:45-62 (Selection.from_pages), row_index.py:20-24
 // (LogicalTopK.from_selection, shared case).
 //
-// Two launches per call:
-//   quest_score_kernel  : HBM-bound streaming pass over min/max [n, Hkv, D];
-//                         one warp per page, lanes own C = ceil(D/32)
-//                         consecutive head-dim elements; fixed fp32 order.
-//   quest_select_kernel : one CTA per request; MSB-first radix select of the
-//                         top_pages largest scores, lower page index first on
-//                         ties; the chosen-page bitmap is scanned in page order
-//                         so the token list comes out sorted.
+// Grid (ctas_per_request, batch). A CTA scores one tile of pages of one
+// request; its work items are (KV head, group of 4 query heads, 8 pages):
+// each lane owns C = ceil(D/32) consecutive head-dim elements, holds its
+// slice of q for the 4 heads in registers, streams the 8 pages' min/max
+// slices, and a 31-shuffle reduce-scatter leaves one (page, head) sum per
+// lane. Head sums meet in shared memory and are combined per page. The last
+// CTA of a request to finish (a completion counter in the workspace) runs the
+// top-k: an MSB-first radix select over order-preserving score keys, then the
+// chosen pages are scanned in page order so tokens come out sorted.
+//
+// Fixed fp32 order (reproducible bit for bit; the oracle restates it):
+//   part[h, j]  = sum over d = j*C .. j*C+C-1 of max(q*min, q*max), left to right
+//   s[h]        = xor tree over lanes j of part[h, j]: pairs (j, j^16), (j^8), ..., (j^1)
+//   u[j]        = sum over heads h = j, j+32, ... of s[h], left to right
+//   score       = (xor tree over j of u[j]) / q_heads
+// For 16-bit q and metadata, max(q*min, q*max) is evaluated as
+// fma(q+, max, .) then fma(q-, min, .) with q+ = max(q, 0), q- = min(q, 0):
+// the products of two 16-bit floats are exact in fp32 and min <= max, so the
+// sums are bit-identical and cost two FFMA per term instead of four ops.
 #include <cstdio>
 
 #include "common.cuh"
@@ -20,198 +31,163 @@
 namespace hs {
 namespace {
 
-constexpr int kScoreThreads = 256;
-constexpr int kScoreWarps = kScoreThreads / 32;
-constexpr int kPagesPerCta = 64;
-constexpr int kSelectThreads = 1024;
+constexpr int kThreads = 128;
+constexpr int kWarps = kThreads / 32;
+constexpr int kHeadsPerItem = 4;
+constexpr int kPagesPerItem = 32 / kHeadsPerItem;  // 8
 
-template <typename TQ, typename TKV> struct QuestScoreParams {
+template <typename TQ, typename TKV> struct QuestParams {
   int batch;
   Batched<TQ> query;
   Batched<TKV> minimum;
   Batched<TKV> maximum;
   Lengths lengths;
-  int q_heads, kv_heads, head_dim, page_size;
+  int q_heads, kv_heads, head_dim, page_size, top_pages, keep_sink;
   int64_t max_pages;
-  float *scores;  // [batch, max_pages]
-  int32_t *status;
-};
-
-// Each lane j owns head-dim elements d = j*C .. j*C+C-1. For a page, lane j
-// computes, for every query head h, part[h] = sum_c max(q*min, q*max) left to
-// right; part[] over the 32 lanes is then reduced with a reduce-scatter whose
-// pairing is (j, j^16), (j, j^8), ..., (j, j^1), which leaves s[h] on lane
-// h % 32. Heads are processed in chunks of 32; lane j accumulates its heads
-// j, j+32, ... left to right and the lanes are finally combined with the
-// same xor tree. The result divided by q_heads is the page score.
-template <typename TQ, typename TKV, int C>
-__global__ void __launch_bounds__(kScoreThreads)
-    quest_score_kernel(QuestScoreParams<TQ, TKV> p) {
-  extern __shared__ float q_smem[];  // [q_heads][32*C], zero padded past head_dim
-  const int b = blockIdx.y;
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int64_t length = p.lengths.at(b);
-  if (length <= 0) return;
-  const int64_t n = ceil_div(length, p.page_size);
-  if (n > p.max_pages) return;  // reported by the select kernel
-  const int64_t page_begin = (int64_t)blockIdx.x * kPagesPerCta;
-  if (page_begin >= n) return;
-  const int64_t page_end = min(n, page_begin + kPagesPerCta);
-
-  const int D = p.head_dim, W = 32 * C;
-  const TQ *q = p.query.at(b);
-  for (int i = threadIdx.x; i < p.q_heads * W; i += blockDim.x) {
-    const int h = i / W, d = i % W;
-    q_smem[i] = d < D ? to_f32(q[(int64_t)h * D + d]) : 0.f;
-  }
-  __syncthreads();
-
-  const TKV *mn_base = p.minimum.at(b);
-  const TKV *mx_base = p.maximum.at(b);
-  const int groups = p.q_heads / p.kv_heads;
-  const int d0 = lane * C;
-  const float inv_heads_div = (float)p.q_heads;
-
-  for (int64_t page = page_begin + warp; page < page_end; page += kScoreWarps) {
-    const int64_t page_off = page * p.kv_heads * D;
-    float u = 0.f;
-    for (int hc = 0; hc < p.q_heads; hc += 32) {
-      float v[32];
-      float mn[C], mx[C];
-      int cur_kh = -1;
-#pragma unroll
-      for (int hl = 0; hl < 32; ++hl) {
-        v[hl] = 0.f;
-        const int h = hc + hl;
-        if (h < p.q_heads) {
-          const int kh = h / groups;
-          if (kh != cur_kh) {
-            cur_kh = kh;
-            const TKV *a = mn_base + page_off + (int64_t)kh * D + d0;
-            const TKV *c = mx_base + page_off + (int64_t)kh * D + d0;
-            if (d0 + C <= D) {
-              const bool al = ((reinterpret_cast<uintptr_t>(a) |
-                                reinterpret_cast<uintptr_t>(c)) &
-                               (C * sizeof(TKV) - 1)) == 0;
-              load_f32<TKV, C>(a, mn, al);
-              load_f32<TKV, C>(c, mx, al);
-            } else {
-#pragma unroll
-              for (int i = 0; i < C; ++i) {
-                mn[i] = d0 + i < D ? to_f32(a[i]) : 0.f;
-                mx[i] = d0 + i < D ? to_f32(c[i]) : 0.f;
-              }
-            }
-          }
-          const float *qh = q_smem + h * W + d0;
-          float part = 0.f;
-#pragma unroll
-          for (int i = 0; i < C; ++i) {
-            if (d0 + i < D) {
-              const float qq = qh[i];
-              const float t = fmaxf(__fmul_rn(qq, mn[i]), __fmul_rn(qq, mx[i]));
-              part = i == 0 ? t : __fadd_rn(part, t);
-            }
-          }
-          v[hl] = part;
-        }
-      }
-      // Reduce-scatter: after the step with offset o, v[0..o) hold the heads
-      // whose bit pattern in [o, 32) equals the lane's.
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) {
-        const bool upper = (lane & o) != 0;
-#pragma unroll
-        for (int i = 0; i < o; ++i) {
-          const float send = upper ? v[i] : v[i + o];
-          const float keep = upper ? v[i + o] : v[i];
-          v[i] = __fadd_rn(keep, __shfl_xor_sync(kFullMask, send, o));
-        }
-      }
-      u = __fadd_rn(u, v[0]);
-    }
-    const float total = warp_xor_tree_sum(u);
-    if (lane == 0) p.scores[(int64_t)b * p.max_pages + page] = __fdiv_rn(total, inv_heads_div);
-  }
-}
-
-struct QuestSelectParams {
-  int batch;
-  Lengths lengths;
-  int page_size, top_pages, keep_sink;
-  int64_t max_pages;
-  const float *scores;
-  int32_t *out_tokens;  // [batch, capacity]
+  int tile_pages;  // pages per CTA (multiple of kPagesPerItem)
+  float *scores;   // workspace [batch, max_pages]
+  unsigned *done;  // workspace [batch] completion counters (zero between calls)
+  int32_t *out_tokens;
   int64_t capacity;
   int32_t *out_counts;
   int32_t *status;
 };
 
-// Order-preserving map of a float score to an unsigned key (larger float ->
-// larger key). -0 is folded onto +0; NaN ranks above +inf (as in torch.topk);
-// forced pages take the maximum key.
+template <typename T> constexpr bool is16() { return sizeof(T) == 2; }
+
+// C consecutive elements of one metadata row, kept in their storage type until
+// use (halves the registers held by in-flight loads for 16-bit metadata).
+template <typename T, int C> struct Raw {
+  T e[C];
+  __device__ __forceinline__ void load(const T *src, bool in, int d0, int D) {
+    constexpr int bytes = C * (int)sizeof(T);
+    if (in && d0 + C <= D) {
+      if constexpr (bytes == 16 || bytes == 8 || bytes == 4) {
+        if ((reinterpret_cast<uintptr_t>(src) & (bytes - 1)) == 0) {
+          if constexpr (bytes == 16) *reinterpret_cast<uint4 *>(e) = __ldg(reinterpret_cast<const uint4 *>(src));
+          if constexpr (bytes == 8) *reinterpret_cast<uint2 *>(e) = __ldg(reinterpret_cast<const uint2 *>(src));
+          if constexpr (bytes == 4) *reinterpret_cast<uint32_t *>(e) = __ldg(reinterpret_cast<const uint32_t *>(src));
+          return;
+        }
+      }
+    }
+#pragma unroll
+    for (int c = 0; c < C; ++c) e[c] = (in && d0 + c < D) ? src[c] : T(0.f);
+  }
+  // Same from a shared-memory address (plain loads: __ldg is global-only).
+  __device__ __forceinline__ void load_shared(const T *src, bool in, int d0, int D) {
+    constexpr int bytes = C * (int)sizeof(T);
+    if (in && d0 + C <= D) {
+      if constexpr (bytes == 16 || bytes == 8 || bytes == 4) {
+        if ((reinterpret_cast<uintptr_t>(src) & (bytes - 1)) == 0) {
+          if constexpr (bytes == 16) *reinterpret_cast<uint4 *>(e) = *reinterpret_cast<const uint4 *>(src);
+          if constexpr (bytes == 8) *reinterpret_cast<uint2 *>(e) = *reinterpret_cast<const uint2 *>(src);
+          if constexpr (bytes == 4) *reinterpret_cast<uint32_t *>(e) = *reinterpret_cast<const uint32_t *>(src);
+          return;
+        }
+      }
+    }
+#pragma unroll
+    for (int c = 0; c < C; ++c) e[c] = (in && d0 + c < D) ? src[c] : T(0.f);
+  }
+  // Whole, aligned row slice from shared memory (the staged path's layout).
+  __device__ __forceinline__ void load_shared_full(const T *src, bool in) {
+    constexpr int bytes = C * (int)sizeof(T);
+    if constexpr (bytes == 16) {
+      *reinterpret_cast<uint4 *>(e) = in ? *reinterpret_cast<const uint4 *>(src) : make_uint4(0, 0, 0, 0);
+    } else if constexpr (bytes == 8) {
+      *reinterpret_cast<uint2 *>(e) = in ? *reinterpret_cast<const uint2 *>(src) : make_uint2(0, 0);
+    } else if constexpr (bytes == 4) {
+      *reinterpret_cast<uint32_t *>(e) = in ? *reinterpret_cast<const uint32_t *>(src) : 0u;
+    } else {
+#pragma unroll
+      for (int c = 0; c < C; ++c) e[c] = in ? src[c] : T(0.f);
+    }
+  }
+  __device__ __forceinline__ void unpack(float (&out)[C]) const {
+#pragma unroll
+    for (int c = 0; c < C; ++c) out[c] = to_f32(e[c]);
+  }
+};
+
+// Order-preserving map of a float score to an unsigned key. -0 is folded onto
+// +0; NaN ranks above +inf (as in torch.topk); forced pages take the maximum.
 __device__ __forceinline__ uint32_t score_key(float s) {
   if (isnan(s)) return 0xfffffffeu;
   const uint32_t bits = __float_as_uint(s + 0.0f);
   return (bits & 0x80000000u) ? ~bits : (bits | 0x80000000u);
 }
 
-__device__ __forceinline__ uint32_t page_key(const QuestSelectParams &p, const float *sc,
-                                             int64_t page, int64_t n, bool sink) {
+__device__ __forceinline__ uint32_t page_key(const float *sc, int64_t page, int64_t n, bool sink) {
   if (page == n - 1 || (sink && page == 0)) return 0xffffffffu;
-  return score_key(sc[page]);
+  return score_key(__ldcg(sc + page));
 }
 
-__global__ void __launch_bounds__(kSelectThreads) quest_select_kernel(QuestSelectParams p) {
+constexpr int kSmemKeys = 16384;  // pages whose keys the select phase caches in shared memory
+
+// Keys of one request: from shared memory when cached, else recomputed from
+// the scores in global memory.
+struct KeySource {
+  const uint32_t *cached;
+  const float *scores;
+  int64_t n;
+  bool sink;
+  __device__ __forceinline__ uint32_t operator()(int64_t page) const {
+    return cached ? cached[page] : page_key(scores, page, n, sink);
+  }
+};
+
+// ---- top-k + expansion for one request (run by the last CTA) ------------------
+template <typename TQ, typename TKV>
+__device__ void select_request(const QuestParams<TQ, TKV> &p, int b, int64_t length, int64_t n,
+                               uint32_t *key_cache) {
   __shared__ uint32_t hist[256];
   __shared__ int64_t scan_scratch[33];
   __shared__ uint32_t s_prefix, s_mask, s_k;
-  const int b = blockIdx.x;
   const int tid = threadIdx.x;
-  const int64_t length = p.lengths.at(b);
   int32_t *out = p.out_tokens + (int64_t)b * p.capacity;
-  const int64_t n = length > 0 ? ceil_div(length, p.page_size) : 0;
   if (length <= 0 || n > p.max_pages) {
     if (n > p.max_pages && tid == 0) flag(p.status, HS_DEV_PAGES_EXCEED_TABLE);
     for (int64_t i = tid; i < p.capacity; i += blockDim.x) out[i] = -1;
     if (tid == 0) p.out_counts[b] = 0;
     return;
   }
-  if (p.top_pages >= n) {
-    // Every page: tokens 0 .. length-1 (selection.py:80-81).
+  if (p.top_pages >= n) {  // every page (selection.py:80-81)
     for (int64_t i = tid; i < p.capacity; i += blockDim.x) out[i] = i < length ? (int32_t)i : -1;
     if (tid == 0) p.out_counts[b] = (int32_t)length;
     return;
   }
   const float *sc = p.scores + (int64_t)b * p.max_pages;
   const bool sink = p.keep_sink && p.top_pages > 1 && n > 1;
-
+  KeySource key_of{nullptr, sc, n, sink};
+  if (key_cache != nullptr && n <= kSmemKeys) {
+    for (int64_t pg = tid; pg < n; pg += blockDim.x) key_cache[pg] = page_key(sc, pg, n, sink);
+    key_of.cached = key_cache;
+  }
   if (tid == 0) {
     s_prefix = 0;
     s_mask = 0;
     s_k = (uint32_t)p.top_pages;
   }
   __syncthreads();
-  // MSB-first radix select of the k-th largest key.
   for (int shift = 24; shift >= 0; shift -= 8) {
     for (int i = tid; i < 256; i += blockDim.x) hist[i] = 0;
     __syncthreads();
     const uint32_t prefix = s_prefix, mask = s_mask;
     for (int64_t pg = tid; pg < n; pg += blockDim.x) {
-      const uint32_t key = page_key(p, sc, pg, n, sink);
+      const uint32_t key = key_of(pg);
       if ((key & mask) == prefix) atomicAdd(&hist[(key >> shift) & 0xffu], 1u);
     }
     __syncthreads();
     if (tid < 32) {
-      // Lane l owns digits [8*(31-l), 8*(31-l)+7]; scanning lanes in order walks
-      // the digits from the top.
+      // lane l owns digits [8*(31-l), 8*(31-l)+7]: lanes in order walk digits from the top
       uint32_t local = 0;
 #pragma unroll
       for (int i = 0; i < 8; ++i) local += hist[8 * (31 - tid) + i];
       const uint32_t inc = warp_inclusive_scan(local);
       const uint32_t k = s_k;
       const unsigned ballot = __ballot_sync(kFullMask, inc >= k);
-      const int owner = __ffs(ballot) - 1;  // first lane whose cumulative count reaches k
+      const int owner = __ffs(ballot) - 1;
       if (tid == owner) {
         uint32_t above = inc - local;
         int digit = 8 * (31 - tid) + 7;
@@ -227,23 +203,19 @@ __global__ void __launch_bounds__(kSelectThreads) quest_select_kernel(QuestSelec
     __syncthreads();
   }
   const uint32_t threshold = s_prefix;
-  const uint32_t take_equal = s_k;  // how many keys == threshold to keep (lowest pages)
-
-  // Pages are split into contiguous runs per thread so scans follow page order.
+  const int64_t take_equal = s_k;  // keys == threshold to keep, lowest pages first
   const int64_t per = ceil_div(n, (int64_t)blockDim.x);
   const int64_t lo = min(n, tid * per), hi = min(n, lo + per);
   int64_t eq_local = 0;
-  for (int64_t pg = lo; pg < hi; ++pg) eq_local += page_key(p, sc, pg, n, sink) == threshold;
+  for (int64_t pg = lo; pg < hi; ++pg) eq_local += key_of(pg) == threshold;
   int64_t eq_total;
-  int64_t eq_before = block_exclusive_scan<int64_t>(eq_local, scan_scratch, &eq_total);
-  // Chosen-page ranks in page order.
+  const int64_t eq_before = block_exclusive_scan<int64_t>(eq_local, scan_scratch, &eq_total);
   int64_t chosen_local = 0;
   {
     int64_t eq = eq_before;
     for (int64_t pg = lo; pg < hi; ++pg) {
-      const uint32_t key = page_key(p, sc, pg, n, sink);
-      const bool take = key > threshold || (key == threshold && eq++ < (int64_t)take_equal);
-      chosen_local += take;
+      const uint32_t key = key_of(pg);
+      chosen_local += key > threshold || (key == threshold && eq++ < take_equal);
     }
   }
   int64_t chosen_total;
@@ -251,9 +223,8 @@ __global__ void __launch_bounds__(kSelectThreads) quest_select_kernel(QuestSelec
   {
     int64_t eq = eq_before;
     for (int64_t pg = lo; pg < hi; ++pg) {
-      const uint32_t key = page_key(p, sc, pg, n, sink);
-      const bool take = key > threshold || (key == threshold && eq++ < (int64_t)take_equal);
-      if (take) {
+      const uint32_t key = key_of(pg);
+      if (key > threshold || (key == threshold && eq++ < take_equal)) {
         const int64_t first = pg * p.page_size;
         const int64_t cnt = min((int64_t)p.page_size, length - first);
         for (int64_t i = 0; i < cnt; ++i) out[rank * p.page_size + i] = (int32_t)(first + i);
@@ -261,25 +232,403 @@ __global__ void __launch_bounds__(kSelectThreads) quest_select_kernel(QuestSelec
       }
     }
   }
-  // Only the tail page (always chosen, always last) can be partial.
+  // only the tail page (always chosen, always last) can be partial
   const int64_t count = (chosen_total - 1) * p.page_size + (length - (n - 1) * p.page_size);
   for (int64_t i = count + tid; i < p.capacity; i += blockDim.x) out[i] = -1;
   if (tid == 0) p.out_counts[b] = (int32_t)count;
 }
 
+// ---- scoring ------------------------------------------------------------------------
+template <typename TQ, typename TKV, int C>
+__global__ void __launch_bounds__(kThreads, 2) quest_kernel(QuestParams<TQ, TKV> p) {
+  extern __shared__ float head_sums[];  // [tile_pages][q_heads]
+  __shared__ int s_last;
+  constexpr bool kFma = is16<TQ>() && is16<TKV>();
+  const int b = blockIdx.y;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int64_t length = p.lengths.at(b);
+  const int64_t n = length > 0 ? ceil_div(length, p.page_size) : 0;
+  const bool score = length > 0 && n <= p.max_pages && p.top_pages < n;
+  const int64_t tile0 = (int64_t)blockIdx.x * p.tile_pages;
+  const int D = p.head_dim, Hq = p.q_heads;
+  if (score && tile0 < n) {
+    const int64_t tile_n = min((int64_t)p.tile_pages, n - tile0);
+    const int groups = Hq / p.kv_heads;
+    const int chunks = (groups + kHeadsPerItem - 1) / kHeadsPerItem;
+    const int page_groups = (int)ceil_div(tile_n, kPagesPerItem);
+    const TQ *q = p.query.at(b);
+    const TKV *mn_base = p.minimum.at(b);
+    const TKV *mx_base = p.maximum.at(b);
+    const int d0 = lane * C;
+    // Each warp keeps one (KV head, head chunk) and its q slice in registers
+    // while it walks the tile's page groups.
+    for (int khc = warp; khc < p.kv_heads * chunks; khc += kWarps) {
+      const int hc = khc % chunks, kh = khc / chunks;
+      const int h_begin = kh * groups + hc * kHeadsPerItem;
+      const int h_count = min(kHeadsPerItem, kh * groups + groups - h_begin);
+      float qa[kHeadsPerItem][C], qb[kHeadsPerItem][C];
+#pragma unroll
+      for (int g = 0; g < kHeadsPerItem; ++g)
+#pragma unroll
+        for (int c = 0; c < C; ++c) {
+          const float v = (g < h_count && d0 + c < D)
+                              ? to_f32(q[(int64_t)(h_begin + g) * D + d0 + c]) : 0.f;
+          qa[g][c] = kFma ? fmaxf(v, 0.f) : v;  // q+ (or q for the exact path)
+          qb[g][c] = kFma ? fminf(v, 0.f) : v;  // q-
+        }
+      for (int pgi = 0; pgi < page_groups; ++pgi) {
+        // the 8 pages' raw min/max slices, all loads issued before any use
+        Raw<TKV, C> lo[kPagesPerItem], hi[kPagesPerItem];
+        const int64_t page0 = tile0 + (int64_t)pgi * kPagesPerItem;
+#pragma unroll
+        for (int i = 0; i < kPagesPerItem; ++i) {
+          const int64_t page = page0 + i;
+          const bool in = page < tile0 + tile_n;
+          const int64_t off = (page * p.kv_heads + kh) * D + d0;
+          lo[i].load(mn_base + off, in, d0, D);
+          hi[i].load(mx_base + off, in, d0, D);
+        }
+        // v[i*4 + g]: this lane's part for (page i, head g)
+        float v[32];
+#pragma unroll
+        for (int i = 0; i < kPagesPerItem; ++i) {
+          float l[C], h[C];
+          lo[i].unpack(l);
+          hi[i].unpack(h);
+#pragma unroll
+          for (int g = 0; g < kHeadsPerItem; ++g) {
+            float part = 0.f;
+#pragma unroll
+            for (int c = 0; c < C; ++c) {
+              if (d0 + c < D) {
+                if constexpr (kFma) {
+                  part = __fmaf_rn(qa[g][c], h[c], c == 0 ? 0.f : part);
+                  part = __fmaf_rn(qb[g][c], l[c], part);
+                } else {
+                  const float t = fmaxf(__fmul_rn(qa[g][c], l[c]), __fmul_rn(qa[g][c], h[c]));
+                  part = c == 0 ? t : __fadd_rn(part, t);
+                }
+              }
+            }
+            v[i * kHeadsPerItem + g] = part;
+          }
+        }
+        // reduce-scatter: after the step with offset o, v[0..o) hold the values
+        // whose index bits in [o, 32) equal the lane's; lane L ends with value L
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+          const bool upper = (lane & o) != 0;
+#pragma unroll
+          for (int i = 0; i < o; ++i) {
+            const float send = upper ? v[i] : v[i + o];
+            const float keep = upper ? v[i + o] : v[i];
+            v[i] = __fadd_rn(keep, __shfl_xor_sync(kFullMask, send, o));
+          }
+        }
+        const int i_page = lane / kHeadsPerItem, g = lane % kHeadsPerItem;
+        const int64_t local_page = (int64_t)pgi * kPagesPerItem + i_page;
+        if (g < h_count && local_page < tile_n) head_sums[local_page * Hq + h_begin + g] = v[0];
+      }
+    }
+    __syncthreads();
+    // per page: lane j adds heads j, j+32, ... then the xor tree; divide by q_heads
+    for (int64_t lp = warp; lp < tile_n; lp += kWarps) {
+      float u = 0.f;
+      for (int h = lane; h < Hq; h += 32) u = __fadd_rn(u, head_sums[lp * Hq + h]);
+      const float total = warp_xor_tree_sum(u);
+      if (lane == 0)
+        p.scores[(int64_t)b * p.max_pages + tile0 + lp] = __fdiv_rn(total, (float)Hq);
+    }
+  }
+  // completion: the last CTA of this request selects
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) s_last = atomicAdd(&p.done[b], 1u) == gridDim.x - 1;
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  select_request(p, b, length, n, reinterpret_cast<uint32_t *>(head_sums));
+  if (threadIdx.x == 0) p.done[b] = 0;  // ready for the next call
+}
+
+// ---- TMA-staged path (16-bit data, page rows a multiple of 16 bytes) ----------
+//
+// One CTA of 16 warps per SM streams a tile of one request's pages through a
+// 3-stage ring of shared-memory buffers. Thread 0 issues, per stage, two 1-D
+// bulk copies (cp.async.bulk, min and max of 16 consecutive pages: one
+// contiguous range each) that complete on the stage's mbarrier; every warp
+// waits on that barrier, computes its (KV head, 4 heads, 8 pages) item from
+// shared memory, and the CTA barrier at the end of a stage hands the buffer
+// back to the producer. The arithmetic and its order are those of
+// quest_kernel; head sums are double buffered so a stage's per-page combine
+// overlaps the next stage's compute.
+constexpr int kTmaThreads = 512;
+constexpr int kTmaWarps = kTmaThreads / 32;
+constexpr int kTmaStagePages = 16;
+constexpr int kTmaStages = 3;
+constexpr long long kWaitLimit = 1ll << 22;  // bounded mbarrier waits (about a second)
+
+__device__ __forceinline__ uint32_t smem_addr(const void *p) {
+  return (uint32_t)__cvta_generic_to_shared(p);
+}
+__device__ __forceinline__ void mbar_init(uint64_t *bar, unsigned count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(smem_addr(bar)), "r"(count));
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, unsigned bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(smem_addr(bar)),
+               "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, unsigned parity) {
+  unsigned done;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+      " selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(done)
+      : "r"(smem_addr(bar)), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+__device__ __forceinline__ void bulk_copy(void *dst, const void *src, unsigned bytes,
+                                          uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n"
+      ::"r"(smem_addr(dst)), "l"(src), "r"(bytes), "r"(smem_addr(bar))
+      : "memory");
+}
+// Waits for `parity` of `bar`; false (and a device flag) when the bounded
+// wait runs out.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, unsigned parity, int32_t *status) {
+  for (long long i = 0; i < kWaitLimit; ++i)
+    if (mbar_try_wait(bar, parity)) return true;
+  flag(status, HS_DEV_WAIT_TIMEOUT);
+  return false;
+}
+
+template <typename TQ, typename TKV, int C>
+__global__ void __launch_bounds__(kTmaThreads, 1) quest_tma_kernel(QuestParams<TQ, TKV> p) {
+  extern __shared__ __align__(128) char smem[];
+  __shared__ __align__(8) uint64_t full[kTmaStages];
+  __shared__ int s_last, s_ok;
+  const int b = blockIdx.y;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int64_t length = p.lengths.at(b);
+  const int64_t n = length > 0 ? ceil_div(length, p.page_size) : 0;
+  const bool score = length > 0 && n <= p.max_pages && p.top_pages < n;
+  const int64_t tile0 = (int64_t)blockIdx.x * p.tile_pages;
+  constexpr int D = 32 * C;  // the staged path requires head_dim == 32 * C
+  const int Hq = p.q_heads, Hkv = p.kv_heads;
+  const int64_t page_elems = (int64_t)Hkv * D;
+  const unsigned page_bytes = (unsigned)(page_elems * sizeof(TKV));
+  const size_t stage_bytes = (size_t)2 * kTmaStagePages * page_bytes;
+  float *sums = reinterpret_cast<float *>(smem + kTmaStages * stage_bytes);  // [2][16][Hq]
+  if (tid == 0) s_ok = 1;
+  if (score && tile0 < n) {
+    const int64_t tile_n = min((int64_t)p.tile_pages, n - tile0);
+    const int nstages = (int)ceil_div(tile_n, kTmaStagePages);
+    const TKV *mn_base = p.minimum.at(b) + tile0 * page_elems;
+    const TKV *mx_base = p.maximum.at(b) + tile0 * page_elems;
+    if (((reinterpret_cast<uintptr_t>(mn_base) | reinterpret_cast<uintptr_t>(mx_base)) & 15) != 0) {
+      // bulk copies need 16-byte aligned sources; the callers guarantee it
+      if (tid == 0) flag(p.status, HS_DEV_MISALIGNED);
+      goto done;
+    }
+    auto issue = [&](int g) {
+      char *buf = smem + (g % kTmaStages) * stage_bytes;
+      const int64_t pages = min((int64_t)kTmaStagePages, tile_n - (int64_t)g * kTmaStagePages);
+      const unsigned bytes = (unsigned)(pages * page_bytes);
+      mbar_expect_tx(&full[g % kTmaStages], 2 * bytes);
+      bulk_copy(buf, mn_base + (int64_t)g * kTmaStagePages * page_elems, bytes,
+                &full[g % kTmaStages]);
+      bulk_copy(buf + kTmaStagePages * page_bytes,
+                mx_base + (int64_t)g * kTmaStagePages * page_elems, bytes, &full[g % kTmaStages]);
+    };
+    if (tid == 0) {
+      for (int s = 0; s < kTmaStages; ++s) mbar_init(&full[s], 1);
+      asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+    }
+    __syncthreads();
+    if (tid == 0)
+      for (int g = 0; g < kTmaStages && g < nstages; ++g) issue(g);
+
+    const int groups = Hq / Hkv;
+    const int chunks = (groups + kHeadsPerItem - 1) / kHeadsPerItem;
+    constexpr int kGroupsPerStage = kTmaStagePages / kPagesPerItem;  // 2
+    const int items = Hkv * chunks * kGroupsPerStage;
+    const TQ *q = p.query.at(b);
+    const int d0 = lane * C;
+    constexpr bool kFma = is16<TQ>() && is16<TKV>();
+    int cur = -1;
+    float qa[kHeadsPerItem][C], qb[kHeadsPerItem][C];
+    for (int g = 0; g < nstages; ++g) {
+      const int64_t pages = min((int64_t)kTmaStagePages, tile_n - (int64_t)g * kTmaStagePages);
+      const char *buf = smem + (g % kTmaStages) * stage_bytes;
+      const TKV *lo_s = reinterpret_cast<const TKV *>(buf);
+      const TKV *hi_s = reinterpret_cast<const TKV *>(buf + kTmaStagePages * page_bytes);
+      float *stage_sums = sums + (g & 1) * kTmaStagePages * Hq;
+      const bool ready = mbar_wait(&full[g % kTmaStages], (g / kTmaStages) & 1, p.status);
+      if (!ready) s_ok = 0;
+      for (int item = warp; ready && item < items; item += kTmaWarps) {
+        const int pgi = item % kGroupsPerStage;
+        const int khc = item / kGroupsPerStage;
+        const int hc = khc % chunks, kh = khc / chunks;
+        const int h_begin = kh * groups + hc * kHeadsPerItem;
+        const int h_count = min(kHeadsPerItem, kh * groups + groups - h_begin);
+        if (khc != cur) {
+          cur = khc;
+#pragma unroll
+          for (int hh = 0; hh < kHeadsPerItem; ++hh)
+#pragma unroll
+            for (int c = 0; c < C; ++c) {
+              const float v = hh < h_count ? to_f32(q[(int64_t)(h_begin + hh) * D + d0 + c]) : 0.f;
+              qa[hh][c] = kFma ? fmaxf(v, 0.f) : v;
+              qb[hh][c] = kFma ? fminf(v, 0.f) : v;
+            }
+        }
+        float v[32];
+#pragma unroll
+        for (int i = 0; i < kPagesPerItem; ++i) {
+          const int lp = pgi * kPagesPerItem + i;
+          float l[C], h[C];
+          Raw<TKV, C> rl, rh;
+          const bool in = lp < pages;
+          rl.load_shared_full(lo_s + lp * (int)page_elems + kh * D + d0, in);
+          rh.load_shared_full(hi_s + lp * (int)page_elems + kh * D + d0, in);
+          rl.unpack(l);
+          rh.unpack(h);
+#pragma unroll
+          for (int hh = 0; hh < kHeadsPerItem; ++hh) {
+            float part = 0.f;
+#pragma unroll
+            for (int c = 0; c < C; ++c) {
+              if constexpr (kFma) {
+                part = __fmaf_rn(qa[hh][c], h[c], c == 0 ? 0.f : part);
+                part = __fmaf_rn(qb[hh][c], l[c], part);
+              } else {
+                const float t = fmaxf(__fmul_rn(qa[hh][c], l[c]), __fmul_rn(qa[hh][c], h[c]));
+                part = c == 0 ? t : __fadd_rn(part, t);
+              }
+            }
+            v[i * kHeadsPerItem + hh] = part;
+          }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+          const bool upper = (lane & o) != 0;
+#pragma unroll
+          for (int i = 0; i < o; ++i) {
+            const float send = upper ? v[i] : v[i + o];
+            const float keep = upper ? v[i + o] : v[i];
+            v[i] = __fadd_rn(keep, __shfl_xor_sync(kFullMask, send, o));
+          }
+        }
+        const int i_page = lane / kHeadsPerItem, hh = lane % kHeadsPerItem;
+        const int lp = pgi * kPagesPerItem + i_page;
+        if (hh < h_count && lp < pages) stage_sums[lp * Hq + h_begin + hh] = v[0];
+      }
+      __syncthreads();  // buffer g % kTmaStages consumed; stage sums complete
+      if (tid == 0 && s_ok && g + kTmaStages < nstages) issue(g + kTmaStages);
+      for (int lp = warp; lp < pages; lp += kTmaWarps) {
+        float u = 0.f;
+        for (int h = lane; h < Hq; h += 32) u = __fadd_rn(u, stage_sums[lp * Hq + h]);
+        const float total = warp_xor_tree_sum(u);
+        if (lane == 0)
+          p.scores[(int64_t)b * p.max_pages + tile0 + (int64_t)g * kTmaStagePages + lp] =
+              __fdiv_rn(total, (float)Hq);
+      }
+      if (!s_ok) {
+        // a copy never completed: wait (bounded) for the stages still in
+        // flight, so no copy lands in shared memory after this CTA exits
+        for (int gg = g + 1; gg < nstages && gg < g + kTmaStages; ++gg)
+          mbar_wait(&full[gg % kTmaStages], (gg / kTmaStages) & 1, p.status);
+        break;
+      }
+    }
+  }
+done:
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) s_last = atomicAdd(&p.done[b], 1u) == gridDim.x - 1;
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  const int64_t cap_keys = (int64_t)(kTmaStages * stage_bytes / sizeof(uint32_t));
+  select_request(p, b, length, n, n <= cap_keys ? reinterpret_cast<uint32_t *>(smem) : nullptr);
+  if (tid == 0) p.done[b] = 0;
+}
+
+int tile_pages_for(int batch, int64_t max_pages) {
+  const int64_t target_ctas = (int64_t)sm_count() * 3 * 2;  // two waves at 3 CTAs per SM
+  int64_t per_req = ceil_div(target_ctas, batch);
+  if (per_req < 1) per_req = 1;
+  int64_t tile = ceil_div(max_pages, per_req);
+  tile = ceil_div(tile, kPagesPerItem) * kPagesPerItem;
+  if (tile < kPagesPerItem) tile = kPagesPerItem;
+  if (tile > 256) tile = 256;
+  return (int)tile;
+}
+
 template <typename TQ, typename TKV>
-int launch_score(const QuestScoreParams<TQ, TKV> &p, int head_dim, cudaStream_t stream) {
-  const int C = (head_dim + 31) / 32;
-  const size_t smem = (size_t)p.q_heads * 32 * C * sizeof(float);
-  dim3 grid((unsigned)ceil_div(p.max_pages, kPagesPerCta), (unsigned)p.batch);
+int launch_tma(QuestParams<TQ, TKV> &p, int C, cudaStream_t stream) {
+  const size_t page_bytes = (size_t)p.kv_heads * p.head_dim * sizeof(TKV);
+  const size_t smem = kTmaStages * 2 * kTmaStagePages * page_bytes +
+                      2 * kTmaStagePages * (size_t)p.q_heads * sizeof(float);
+  int64_t per_req = sm_count() / p.batch;
+  if (per_req < 1) per_req = 1;
+  int64_t tile = ceil_div(p.max_pages, per_req);
+  tile = ceil_div(tile, kTmaStagePages) * kTmaStagePages;
+  p.tile_pages = (int)tile;
+  dim3 grid((unsigned)ceil_div(p.max_pages, tile), (unsigned)p.batch);
+#define HS_QUEST_TMA(CC)                                                                  \
+  case CC: {                                                                              \
+    auto k = quest_tma_kernel<TQ, TKV, CC>;                                               \
+    if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != \
+        cudaSuccess)                                                                      \
+      return set_error(HS_ERR_CUDA, "quest: cannot reserve %zu bytes of shared memory", smem); \
+    k<<<grid, kTmaThreads, smem, stream>>>(p);                                            \
+    break;                                                                                \
+  }
+  switch (C) {
+    HS_QUEST_TMA(1)
+    HS_QUEST_TMA(2)
+    HS_QUEST_TMA(4)
+    default:
+      return set_error(HS_ERR_UNSUPPORTED, "quest: no staged path for head_dim %d", p.head_dim);
+  }
+#undef HS_QUEST_TMA
+  return check_launch("quest_tma_kernel");
+}
+
+// The staged path needs whole 16-byte page rows, 16-byte aligned metadata and
+// a ring that fits shared memory; other shapes use quest_kernel.
+template <typename TQ, typename TKV>
+bool tma_eligible(const QuestParams<TQ, TKV> &p, bool aligned) {
+  const int C = (p.head_dim + 31) / 32;
+  const size_t page_bytes = (size_t)p.kv_heads * p.head_dim * sizeof(TKV);
+  const size_t smem = kTmaStages * 2 * kTmaStagePages * page_bytes +
+                      2 * kTmaStagePages * (size_t)p.q_heads * sizeof(float);
+  return aligned && page_bytes % 16 == 0 && smem <= 200 * 1024 && (C == 1 || C == 2 || C == 4) &&
+         p.head_dim % C == 0 && p.head_dim == 32 * C;
+}
+
+template <typename TQ, typename TKV>
+int launch(QuestParams<TQ, TKV> &p, cudaStream_t stream, bool aligned) {
+  const int C = (p.head_dim + 31) / 32;
+  if (tma_eligible(p, aligned)) return launch_tma(p, C, stream);
+  p.tile_pages = tile_pages_for(p.batch, p.max_pages);
+  const size_t sums_bytes = (size_t)p.tile_pages * p.q_heads * sizeof(float);
+  const size_t keys_bytes =
+      (size_t)(p.max_pages < kSmemKeys ? p.max_pages : kSmemKeys) * sizeof(uint32_t);
+  const size_t smem = sums_bytes > keys_bytes ? sums_bytes : keys_bytes;
+  dim3 grid((unsigned)ceil_div(p.max_pages, p.tile_pages), (unsigned)p.batch);
 #define HS_QUEST_CASE(CC)                                                                 \
   case CC: {                                                                              \
-    auto k = quest_score_kernel<TQ, TKV, CC>;                                             \
+    auto k = quest_kernel<TQ, TKV, CC>;                                                   \
     if (smem > 48 * 1024 &&                                                               \
         cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != \
             cudaSuccess)                                                                  \
       return set_error(HS_ERR_CUDA, "quest: cannot reserve %zu bytes of shared memory", smem); \
-    k<<<grid, kScoreThreads, smem, stream>>>(p);                                          \
+    k<<<grid, kThreads, smem, stream>>>(p);                                               \
     break;                                                                                \
   }
   switch (C) {
@@ -292,113 +641,100 @@ int launch_score(const QuestScoreParams<TQ, TKV> &p, int head_dim, cudaStream_t 
     HS_QUEST_CASE(7)
     HS_QUEST_CASE(8)
     default:
-      return set_error(HS_ERR_UNSUPPORTED, "quest: head_dim %d > 256 is not supported", head_dim);
+      return set_error(HS_ERR_UNSUPPORTED, "quest: head_dim %d > 256 is not supported",
+                       p.head_dim);
   }
 #undef HS_QUEST_CASE
-  return check_launch("quest_score_kernel");
+  return check_launch("quest_kernel");
 }
 
-template <typename TQ>
-int dispatch_kv(int kv_dtype, const void *query, int64_t qstride, const void *mn,
-                const void *mx, const uint64_t *mn_ptrs, const uint64_t *mx_ptrs,
-                QuestScoreParams<float, float> proto, int head_dim, cudaStream_t stream) {
-  auto fill = [&](auto tag) {
-    using TKV = decltype(tag);
-    QuestScoreParams<TQ, TKV> p;
-    p.batch = proto.batch;
-    p.query = Batched<TQ>{static_cast<const TQ *>(query), qstride, nullptr};
-    p.minimum = Batched<TKV>{static_cast<const TKV *>(mn), 0, mn_ptrs};
-    p.maximum = Batched<TKV>{static_cast<const TKV *>(mx), 0, mx_ptrs};
-    p.lengths = proto.lengths;
-    p.q_heads = proto.q_heads;
-    p.kv_heads = proto.kv_heads;
-    p.head_dim = proto.head_dim;
-    p.page_size = proto.page_size;
-    p.max_pages = proto.max_pages;
-    p.scores = proto.scores;
-    p.status = proto.status;
-    return launch_score<TQ, TKV>(p, head_dim, stream);
-  };
-  switch (kv_dtype) {
-    case HS_FLOAT32: return fill(float{});
-    case HS_FLOAT16: return fill(__half{});
-    case HS_BFLOAT16: return fill(__nv_bfloat16{});
+struct Common {
+  int batch;
+  const void *query;
+  int64_t qstride;
+  int query_dtype;
+  const void *mn, *mx;
+  const uint64_t *mn_ptrs, *mx_ptrs;
+  int kv_dtype;
+  Lengths lengths;
+  int q_heads, kv_heads, head_dim, page_size, top_pages, keep_sink;
+  int64_t max_pages;
+  int32_t *out_tokens;
+  int64_t capacity;
+  int32_t *out_counts;
+  void *workspace;
+  size_t workspace_bytes;
+  int32_t *status;
+};
+
+template <typename TQ, typename TKV> int run(const Common &c, cudaStream_t stream) {
+  QuestParams<TQ, TKV> p;
+  p.batch = c.batch;
+  p.query = Batched<TQ>{static_cast<const TQ *>(c.query), c.qstride, nullptr};
+  p.minimum = Batched<TKV>{static_cast<const TKV *>(c.mn), 0, c.mn_ptrs};
+  p.maximum = Batched<TKV>{static_cast<const TKV *>(c.mx), 0, c.mx_ptrs};
+  p.lengths = c.lengths;
+  p.q_heads = c.q_heads;
+  p.kv_heads = c.kv_heads;
+  p.head_dim = c.head_dim;
+  p.page_size = c.page_size;
+  p.top_pages = c.top_pages;
+  p.keep_sink = c.keep_sink;
+  p.max_pages = c.max_pages;
+  p.scores = static_cast<float *>(c.workspace);
+  p.done = reinterpret_cast<unsigned *>(static_cast<char *>(c.workspace) +
+                                        (size_t)c.batch * c.max_pages * sizeof(float));
+  p.out_tokens = c.out_tokens;
+  p.capacity = c.capacity;
+  p.out_counts = c.out_counts;
+  p.status = c.status;
+  // pointer arrays (batched calls) are required to be 16-byte aligned
+  const bool aligned = c.mn_ptrs != nullptr ||
+                       ((reinterpret_cast<uintptr_t>(c.mn) | reinterpret_cast<uintptr_t>(c.mx)) &
+                        15) == 0;
+  return launch<TQ, TKV>(p, stream, aligned);
+}
+
+template <typename TQ> int dispatch_kv(const Common &c, cudaStream_t s) {
+  switch (c.kv_dtype) {
+    case HS_FLOAT32: return run<TQ, float>(c, s);
+    case HS_FLOAT16: return run<TQ, __half>(c, s);
+    case HS_BFLOAT16: return run<TQ, __nv_bfloat16>(c, s);
   }
-  return set_error(HS_ERR_INVALID_ARGUMENT, "quest: invalid KV dtype %d", kv_dtype);
+  return set_error(HS_ERR_INVALID_ARGUMENT, "quest: invalid KV dtype %d", c.kv_dtype);
 }
 
-int quest_common(int batch, const void *query, int64_t qstride, int query_dtype,
-                 const void *mn, const void *mx, const uint64_t *mn_ptrs,
-                 const uint64_t *mx_ptrs, int kv_dtype, Lengths lengths, int q_heads,
-                 int kv_heads, int head_dim, int64_t max_pages, int page_size,
-                 int top_pages, int keep_sink, int32_t *out_tokens, int64_t capacity,
-                 int32_t *out_counts, void *workspace, size_t workspace_bytes,
-                 int32_t *status, cudaStream_t stream) {
-  if (batch < 1 || q_heads < 1 || kv_heads < 1 || head_dim < 1 || page_size < 1 ||
-      max_pages < 1)
+int quest_common(const Common &c, cudaStream_t stream) {
+  if (c.batch < 1 || c.q_heads < 1 || c.kv_heads < 1 || c.head_dim < 1 || c.page_size < 1 ||
+      c.max_pages < 1)
     return set_error(HS_ERR_INVALID_ARGUMENT, "quest: dimensions must be positive");
-  if (top_pages < 1 || q_heads % kv_heads)
+  if (c.top_pages < 1 || c.q_heads % c.kv_heads)
     return set_error(HS_ERR_INVALID_ARGUMENT, "invalid page budget or GQA shape");
-  if (head_dim > 256)
-    return set_error(HS_ERR_UNSUPPORTED, "quest: head_dim %d > 256 is not supported", head_dim);
-  if ((size_t)q_heads * 32 * ((head_dim + 31) / 32) * sizeof(float) > 200 * 1024)
-    return set_error(HS_ERR_UNSUPPORTED, "quest: query of %d heads does not fit shared memory",
-                     q_heads);
-  if (!query || !out_tokens || !out_counts || (!mn && !mn_ptrs) || (!mx && !mx_ptrs))
+  if (c.head_dim > 256)
+    return set_error(HS_ERR_UNSUPPORTED, "quest: head_dim %d > 256 is not supported",
+                     c.head_dim);
+  if (!c.query || !c.out_tokens || !c.out_counts || (!c.mn && !c.mn_ptrs) ||
+      (!c.mx && !c.mx_ptrs))
     return set_error(HS_ERR_INVALID_ARGUMENT, "quest: null tensor pointer");
-  if (capacity < (int64_t)top_pages * page_size)
+  if (c.capacity < (int64_t)c.top_pages * c.page_size)
     return set_error(HS_ERR_INVALID_ARGUMENT,
                      "quest: out_capacity %lld < top_pages * page_size = %lld",
-                     (long long)capacity, (long long)top_pages * page_size);
-  if (capacity > INT32_MAX || max_pages * (int64_t)page_size > INT32_MAX)
+                     (long long)c.capacity, (long long)c.top_pages * c.page_size);
+  if (c.capacity > INT32_MAX || c.max_pages * (int64_t)c.page_size > INT32_MAX)
     return set_error(HS_ERR_INVALID_ARGUMENT, "quest: token positions must fit int32");
-  const size_t need = hs_quest_workspace_bytes(batch, max_pages);
-  if (!workspace || workspace_bytes < need)
+  if ((size_t)tile_pages_for(c.batch, c.max_pages) * c.q_heads * sizeof(float) > 200 * 1024)
+    return set_error(HS_ERR_UNSUPPORTED, "quest: %d query heads do not fit shared memory",
+                     c.q_heads);
+  const size_t need = hs_quest_workspace_bytes(c.batch, c.max_pages);
+  if (!c.workspace || c.workspace_bytes < need)
     return set_error(HS_ERR_WORKSPACE, "quest: workspace of %zu bytes < required %zu",
-                     workspace_bytes, need);
-  float *scores = static_cast<float *>(workspace);
-  QuestScoreParams<float, float> proto;
-  proto.batch = batch;
-  proto.lengths = lengths;
-  proto.q_heads = q_heads;
-  proto.kv_heads = kv_heads;
-  proto.head_dim = head_dim;
-  proto.page_size = page_size;
-  proto.max_pages = max_pages;
-  proto.scores = scores;
-  proto.status = status;
-  int rc;
-  switch (query_dtype) {
-    case HS_FLOAT32:
-      rc = dispatch_kv<float>(kv_dtype, query, qstride, mn, mx, mn_ptrs, mx_ptrs, proto,
-                              head_dim, stream);
-      break;
-    case HS_FLOAT16:
-      rc = dispatch_kv<__half>(kv_dtype, query, qstride, mn, mx, mn_ptrs, mx_ptrs, proto,
-                               head_dim, stream);
-      break;
-    case HS_BFLOAT16:
-      rc = dispatch_kv<__nv_bfloat16>(kv_dtype, query, qstride, mn, mx, mn_ptrs, mx_ptrs,
-                                      proto, head_dim, stream);
-      break;
-    default:
-      return set_error(HS_ERR_INVALID_ARGUMENT, "quest: invalid query dtype %d", query_dtype);
+                     c.workspace_bytes, need);
+  switch (c.query_dtype) {
+    case HS_FLOAT32: return dispatch_kv<float>(c, stream);
+    case HS_FLOAT16: return dispatch_kv<__half>(c, stream);
+    case HS_BFLOAT16: return dispatch_kv<__nv_bfloat16>(c, stream);
   }
-  if (rc != HS_OK) return rc;
-  QuestSelectParams s;
-  s.batch = batch;
-  s.lengths = lengths;
-  s.page_size = page_size;
-  s.top_pages = top_pages;
-  s.keep_sink = keep_sink;
-  s.max_pages = max_pages;
-  s.scores = scores;
-  s.out_tokens = out_tokens;
-  s.capacity = capacity;
-  s.out_counts = out_counts;
-  s.status = status;
-  quest_select_kernel<<<batch, kSelectThreads, 0, stream>>>(s);
-  return check_launch("quest_select_kernel");
+  return set_error(HS_ERR_INVALID_ARGUMENT, "quest: invalid query dtype %d", c.query_dtype);
 }
 
 }  // namespace
@@ -406,7 +742,8 @@ int quest_common(int batch, const void *query, int64_t qstride, int query_dtype,
 
 extern "C" size_t hs_quest_workspace_bytes(int batch, int64_t max_pages) {
   if (batch < 1 || max_pages < 1) return 0;
-  return (size_t)batch * (size_t)max_pages * sizeof(float);
+  // scores [batch, max_pages] fp32, then one completion counter per request
+  return (size_t)batch * (size_t)max_pages * sizeof(float) + (size_t)batch * sizeof(unsigned);
 }
 
 extern "C" int hs_quest_select(const void *query, int query_dtype, const void *minimum,
@@ -423,11 +760,11 @@ extern "C" int hs_quest_select(const void *query, int query_dtype, const void *m
                          "quest: ceil(length / page_size) exceeds the metadata pages");
   if (!minimum || !maximum)
     return hs::set_error(HS_ERR_INVALID_ARGUMENT, "quest: null metadata pointer");
-  return hs::quest_common(1, query, 0, query_dtype, minimum, maximum, nullptr, nullptr,
-                          kv_dtype, hs::Lengths{nullptr, length}, q_heads, kv_heads,
-                          head_dim, max_pages, page_size, top_pages, keep_sink, out_tokens,
-                          out_capacity, out_count, workspace, workspace_bytes,
-                          device_status, static_cast<cudaStream_t>(stream));
+  hs::Common c{1, query, 0, query_dtype, minimum, maximum, nullptr, nullptr, kv_dtype,
+               hs::Lengths{nullptr, length}, q_heads, kv_heads, head_dim, page_size,
+               top_pages, keep_sink, max_pages, out_tokens, out_capacity, out_count,
+               workspace, workspace_bytes, device_status};
+  return hs::quest_common(c, static_cast<cudaStream_t>(stream));
 }
 
 extern "C" int hs_quest_select_batched(int batch, const void *query,
@@ -442,10 +779,9 @@ extern "C" int hs_quest_select_batched(int batch, const void *query,
                                        int32_t *device_status, hs_stream stream) {
   if (!minimum_ptrs || !maximum_ptrs || !lengths)
     return hs::set_error(HS_ERR_INVALID_ARGUMENT, "quest: null pointer array or lengths");
-  return hs::quest_common(batch, query, query_batch_stride, query_dtype, nullptr, nullptr,
-                          minimum_ptrs, maximum_ptrs, kv_dtype, hs::Lengths{lengths, 0},
-                          q_heads, kv_heads, head_dim, max_pages, page_size, top_pages,
-                          keep_sink, out_tokens, out_capacity, out_counts, workspace,
-                          workspace_bytes, device_status,
-                          static_cast<cudaStream_t>(stream));
+  hs::Common c{batch, query, query_batch_stride, query_dtype, nullptr, nullptr, minimum_ptrs,
+               maximum_ptrs, kv_dtype, hs::Lengths{lengths, 0}, q_heads, kv_heads, head_dim,
+               page_size, top_pages, keep_sink, max_pages, out_tokens, out_capacity,
+               out_counts, workspace, workspace_bytes, device_status};
+  return hs::quest_common(c, static_cast<cudaStream_t>(stream));
 }

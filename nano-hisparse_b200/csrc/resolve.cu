@@ -47,7 +47,7 @@ __host__ __device__ inline size_t align16(size_t x) { return (x + 15) & ~size_t(
 
 struct Layout {
   int64_t kp, ch;  // padded sort length, hash capacity
-  size_t keys, first, flags, slot, host, phys, hash, sflags, lru_old, victims, total;
+  size_t keys, first, flags, slot, rank, host, phys, hash, sflags, lru_old, victims, total;
   __host__ __device__ Layout(int64_t k, int64_t h) {
     kp = next_pow2(k);
     ch = next_pow2(2 * h);
@@ -57,6 +57,7 @@ struct Layout {
     first = o;   o = align16(o + k * 4);
     flags = o;   o = align16(o + k);
     slot = o;    o = align16(o + k * 4);
+    rank = o;    o = align16(o + k * 4);
     host = o;    o = align16(o + k * 8);
     phys = o;    o = align16(o + k * 8);
     hash = o;    o = align16(o + ch * 8);
@@ -108,13 +109,13 @@ __device__ __forceinline__ void hash_insert(unsigned long long *table, int64_t c
   }
 }
 
-__device__ __forceinline__ int64_t hash_find(const unsigned long long *table, int64_t ch,
-                                             uint32_t key) {
+__device__ __forceinline__ int hash_find(const unsigned long long *table, int64_t ch,
+                                         uint32_t key) {
   uint32_t h = hash_slot(key, ch);
   while (true) {
     const unsigned long long cur = table[h];
     if (cur == kEmpty) return -1;
-    if ((uint32_t)(cur >> 32) == key) return h;
+    if ((uint32_t)(cur >> 32) == key) return (int)h;
     h = (h + 1) & (uint32_t)(ch - 1);
   }
 }
@@ -126,36 +127,30 @@ __device__ __forceinline__ int64_t load_position(const ResolveParams &p, int b, 
 }
 
 // Smallest j in [0, n) with keys[j] >= v (n if none).
-__device__ __forceinline__ int64_t lower_bound(const int32_t *keys, int64_t n, int64_t v) {
-  int64_t lo = 0, hi = n;
+__device__ __forceinline__ int lower_bound(const int32_t *keys, int n, int64_t v) {
+  int lo = 0, hi = n;
   while (lo < hi) {
-    const int64_t mid = (lo + hi) >> 1;
+    const int mid = (lo + hi) >> 1;
     if ((int64_t)keys[mid] < v) lo = mid + 1; else hi = mid;
   }
   return lo;
 }
 
-__global__ void __launch_bounds__(kResolveThreads) resolve_kernel(ResolveParams p) {
-  extern __shared__ __align__(16) char smem_raw[];
-  __shared__ int64_t scan_scratch[33];
-  __shared__ int s_abort;
-  __shared__ unsigned long long s_counts[3];
-  const int b = blockIdx.x;
-  const int tid = threadIdx.x, nthreads = blockDim.x;
-  const int64_t K = p.count, H = p.hot_rows;
-  const Layout L(K, H);
-  char *base = p.workspace ? p.workspace + (size_t)b * L.total : smem_raw;
-  int32_t *keys = reinterpret_cast<int32_t *>(base + L.keys);
-  int32_t *first_in = reinterpret_cast<int32_t *>(base + L.first);
-  uint8_t *jflags = reinterpret_cast<uint8_t *>(base + L.flags);
-  int32_t *jslot = reinterpret_cast<int32_t *>(base + L.slot);
-  int64_t *jhost = reinterpret_cast<int64_t *>(base + L.host);
-  int64_t *jphys = reinterpret_cast<int64_t *>(base + L.phys);
-  unsigned long long *table = reinterpret_cast<unsigned long long *>(base + L.hash);
-  uint8_t *sflags = reinterpret_cast<uint8_t *>(base + L.sflags);
-  int32_t *lru_old = reinterpret_cast<int32_t *>(base + L.lru_old);
-  int32_t *victims = reinterpret_cast<int32_t *>(base + L.victims);
+// Packed counters for one scan: misses in bits 0-20, hot hits 21-41, resident
+// hits 42-62 (count < 2^21, checked on the host).
+constexpr int kCountBits = 21;
+constexpr unsigned long long kCountMask = (1ull << kCountBits) - 1;
 
+// Steps 3-9 of resolve_kernel (every thread of the block calls it).
+__device__ __forceinline__ void resolve_body(const ResolveParams &p, const Layout &L, int b,
+                                          bool sorted, int32_t *keys, int32_t *first_in,
+                                          uint8_t *jflags, int32_t *jslot, int32_t *jrank,
+                                          int64_t *jhost, int64_t *jphys,
+                                          unsigned long long *table, uint8_t *sflags,
+                                          int32_t *lru_old, int32_t *victims,
+                                          unsigned long long *scan_scratch) {
+  const int tid = threadIdx.x, nthreads = blockDim.x;
+  const int K = (int)p.count, H = (int)p.hot_rows;
   const int32_t *src_tab = p.source.at(b);
   const int32_t *res_tab = p.resident.at(b);
   const int32_t *hot_tab = p.hot.at(b);
@@ -167,61 +162,12 @@ __global__ void __launch_bounds__(kResolveThreads) resolve_kernel(ResolveParams 
   int64_t *out_mh = p.out_miss_host + (int64_t)b * K;
   int64_t *out_md = p.out_miss_device + (int64_t)b * K;
   int64_t *out_counts = p.out_counts + (int64_t)b * 3;
-
-  if (tid == 0) {
-    s_abort = 0;
-    s_counts[0] = s_counts[1] = s_counts[2] = 0;
-  }
-  // ---- 1. load and normalise; clear scratch -----------------------------------
-  for (int64_t i = tid; i < L.kp; i += nthreads) {
-    int32_t v = INT32_MAX;
-    if (i < K) {
-      const int64_t raw = load_position(p, b, i);
-      v = (int32_t)((raw >= 0 && raw < length) ? raw : length);
-      first_in[i] = (int32_t)K;
-    }
-    keys[i] = v;
-  }
-  for (int64_t s = tid; s < L.ch; s += nthreads) table[s] = kEmpty;
-  __syncthreads();
-  for (int64_t s = tid; s < H; s += nthreads) {
-    sflags[s] = 0;
-    const int64_t v = lru[s];
-    if (v < 0 || v >= H) s_abort = 1;
-    lru_old[s] = (int32_t)v;
-  }
-  // ---- 2. bitonic sort of keys[0, kp) ascending ---------------------------------
-  for (int64_t k = 2; k <= L.kp; k <<= 1) {
-    for (int64_t j = k >> 1; j > 0; j >>= 1) {
-      __syncthreads();
-      for (int64_t i = tid; i < L.kp; i += nthreads) {
-        const int64_t l = i ^ j;
-        if (l > i) {
-          const int32_t a = keys[i], c = keys[l];
-          const bool up = (i & k) == 0;
-          if ((a > c) == up) {
-            keys[i] = c;
-            keys[l] = a;
-          }
-        }
-      }
-    }
-  }
-  __syncthreads();
-  if (s_abort) {
-    // A corrupt LRU permutation cannot be resolved faithfully: leave the
-    // tables untouched and return an empty plan.
-    for (int64_t i = tid; i < K; i += nthreads) out_phys[i] = out_mh[i] = out_md[i] = -1;
-    if (tid < 3) out_counts[tid] = 0;
-    if (tid == 0) flag(p.status, HS_DEV_LRU_CORRUPT);
-    goto head_columns;
-  }
-  // ---- 3. first occurrence in input order; per-entry lookups; tag hash ---------
-  for (int64_t i = tid; i < K; i += nthreads) {
-    const int64_t raw = load_position(p, b, i);
-    if (raw >= 0 && raw < length) atomicMin(&first_in[lower_bound(keys, K, raw)], (int32_t)i);
-  }
-  for (int64_t j = tid; j < K; j += nthreads) {
+  const int per_k = (K + nthreads - 1) / nthreads;
+  const int klo = min(K, tid * per_k), khi = min(K, klo + per_k);
+  const int per_h = (H + nthreads - 1) / nthreads;
+  const int hlo = min(H, tid * per_h), hhi = min(H, hlo + per_h);
+  // ---- 3. per sorted entry: dedupe and page lookups; hash of the hot tags ------
+  for (int j = tid; j < K; j += nthreads) {
     const int64_t v = keys[j];
     const bool unique = v < length && (j == 0 || keys[j - 1] != keys[j]);
     int64_t page = v / P;
@@ -229,7 +175,6 @@ __global__ void __launch_bounds__(kResolveThreads) resolve_kernel(ResolveParams 
     const int64_t offset = v % P;
     const int64_t source = src_tab[page];
     const int64_t resident = res_tab[page];
-    const int64_t host = source * P + offset;
     uint8_t f = 0;
     int64_t phys = -1;
     if (unique && source >= 0) {
@@ -242,21 +187,21 @@ __global__ void __launch_bounds__(kResolveThreads) resolve_kernel(ResolveParams 
       }
     }
     jflags[j] = f;
-    jhost[j] = host;
+    jhost[j] = source * P + offset;
     jphys[j] = phys;
   }
-  for (int64_t s = tid; s < H; s += nthreads) {
+  for (int s = tid; s < H; s += nthreads) {
     const int32_t t = tags[s];
     if (t >= 0) hash_insert(table, L.ch, (uint32_t)t, (uint32_t)s);
   }
   __syncthreads();
-  // ---- 4. hot-hit lookup; mark wanted tags ---------------------------------------
-  for (int64_t j = tid; j < K; j += nthreads) {
+  // ---- 4. hot hits; tags wanted by this selection ---------------------------------
+  for (int j = tid; j < K; j += nthreads) {
     uint8_t f = jflags[j];
     if (f & kNeedsHot) {
       const int64_t host = jhost[j];
-      int64_t at = -1;
-      if (host >= 0 && host <= INT32_MAX) at = hash_find(table, L.ch, (uint32_t)host);
+      const int at = (host >= 0 && host <= INT32_MAX) ? hash_find(table, L.ch, (uint32_t)host)
+                                                       : -1;
       if (at >= 0) {
         f |= kHotHit;
         jslot[j] = (int32_t)(table[at] & 0x7fffffffu);
@@ -268,113 +213,93 @@ __global__ void __launch_bounds__(kResolveThreads) resolve_kernel(ResolveParams 
     }
   }
   __syncthreads();
-  // ---- 5. protected slots; miss ranks (sorted logical order) --------------------
-  for (int64_t s = tid; s < H; s += nthreads) {
+  // ---- 5. protected slots; packed counts and miss ranks (sorted logical order) ----
+  for (int s = tid; s < H; s += nthreads) {
     const int32_t t = tags[s];
     if (t >= 0) {
-      const int64_t at = hash_find(table, L.ch, (uint32_t)t);
+      const int at = hash_find(table, L.ch, (uint32_t)t);
       if (at >= 0 && (table[at] & kWantedBit)) sflags[s] = kProtected;
     }
   }
-  int64_t misses;
+  unsigned long long totals;
   {
-    const int64_t per = ceil_div(K, nthreads);
-    const int64_t lo = min(K, tid * per), hi = min(K, lo + per);
-    int64_t local = 0;
-    for (int64_t j = lo; j < hi; ++j) local += (jflags[j] & kMiss) != 0;
-    int64_t rank = block_exclusive_scan<int64_t>(local, scan_scratch, &misses);
-    for (int64_t j = lo; j < hi; ++j)
-      if (jflags[j] & kMiss) jslot[j] = (int32_t)(rank++);  // temporarily the miss rank
+    unsigned long long local = 0;
+    for (int j = klo; j < khi; ++j) {
+      const uint8_t f = jflags[j];
+      local += (f & kMiss) ? 1ull : (f & kHotHit) ? (1ull << kCountBits)
+               : (f & kResidentHit) ? (1ull << (2 * kCountBits)) : 0ull;
+    }
+    unsigned long long prefix = block_exclusive_scan<unsigned long long>(local, scan_scratch,
+                                                                        &totals);
+    int rank = (int)(prefix & kCountMask);
+    for (int j = klo; j < khi; ++j)
+      if (jflags[j] & kMiss) jrank[j] = rank++;
   }
-  // ---- 6. victims: unprotected slots in LRU order, then protected ----------------
+  const int misses = (int)(totals & kCountMask);
+  // ---- 6. victims: unprotected slots in LRU order, then protected ---------------
   {
-    const int64_t per = ceil_div(H, nthreads);
-    const int64_t lo = min(H, tid * per), hi = min(H, lo + per);
-    int64_t local = 0;
-    for (int64_t i = lo; i < hi; ++i) local += !(sflags[lru_old[i]] & kProtected);
-    int64_t unprotected;
-    int64_t pos = block_exclusive_scan<int64_t>(local, scan_scratch, &unprotected);
-    for (int64_t i = lo; i < hi; ++i) {
+    unsigned long long local = 0;
+    for (int i = hlo; i < hhi; ++i) local += !(sflags[lru_old[i]] & kProtected);
+    unsigned long long unprotected;
+    int pos = (int)block_exclusive_scan<unsigned long long>(local, scan_scratch, &unprotected);
+    for (int i = hlo; i < hhi; ++i) {
       const int32_t s = lru_old[i];
       if (!(sflags[s] & kProtected)) victims[pos++] = s;
-      else victims[unprotected + (i - pos)] = s;
+      else victims[(int)unprotected + (i - pos)] = s;
     }
   }
   __syncthreads();
   if (misses > H) {
-    // Only reachable with more positions than hot rows (the cache caps
-    // positions at max_union_rows <= hot_rows).
-    for (int64_t i = tid; i < K; i += nthreads) out_phys[i] = out_mh[i] = out_md[i] = -1;
+    // only reachable with more positions than hot rows (the cache caps
+    // positions at max_union_rows <= hot_rows)
+    for (int i = tid; i < K; i += nthreads) out_phys[i] = out_mh[i] = out_md[i] = -1;
     if (tid < 3) out_counts[tid] = 0;
     if (tid == 0) flag(p.status, HS_DEV_MISSES_EXCEED_HOT);
-    goto head_columns;
+    return;
   }
   // ---- 7. slots, physical rows, miss plan, tag update -----------------------------
-  {
-    unsigned long long c_res = 0, c_hot = 0, c_miss = 0;
-    for (int64_t j = tid; j < K; j += nthreads) {
-      const uint8_t f = jflags[j];
-      c_res += (f & kResidentHit) != 0;
-      if (!(f & kNeedsHot)) continue;
-      int32_t slot;
-      if (f & kMiss) {
-        const int32_t rank = jslot[j];
-        slot = victims[rank];
-        jslot[j] = slot;
-        sflags[slot] |= kInserted;
-        ++c_miss;
-      } else {
-        slot = jslot[j];
-        ++c_hot;
-      }
-      const int64_t block = hot_tab[slot / P];
-      const int64_t hot_phys = block * P + slot % P;
-      jphys[j] = hot_phys;
+  for (int j = tid; j < K; j += nthreads) {
+    const uint8_t f = jflags[j];
+    if (!(f & kNeedsHot)) continue;
+    int32_t slot;
+    if (f & kMiss) {
+      slot = victims[jrank[j]];
+      sflags[slot] |= kInserted;
+    } else {
+      slot = jslot[j];
     }
-    atomicAdd(&s_counts[0], c_res);
-    atomicAdd(&s_counts[1], c_hot);
-    atomicAdd(&s_counts[2], c_miss);
-  }
-  __syncthreads();
-  {
-    // Miss plan: the miss ranks were consumed above, so rebuild them with the
-    // same scan (deterministic) and write entries in sorted logical order.
-    const int64_t per = ceil_div(K, nthreads);
-    const int64_t lo = min(K, tid * per), hi = min(K, lo + per);
-    int64_t local = 0;
-    for (int64_t j = lo; j < hi; ++j) local += (jflags[j] & kMiss) != 0;
-    int64_t total;
-    int64_t rank = block_exclusive_scan<int64_t>(local, scan_scratch, &total);
-    for (int64_t j = lo; j < hi; ++j) {
-      if (jflags[j] & kMiss) {
-        out_mh[rank] = jhost[j];
-        out_md[rank] = jphys[j];
-        tags[jslot[j]] = (int32_t)jhost[j];
-        ++rank;
-      }
+    const int64_t hot_phys = (int64_t)hot_tab[slot / P] * P + slot % P;
+    jphys[j] = hot_phys;
+    if (f & kMiss) {
+      const int r = jrank[j];
+      out_mh[r] = jhost[j];
+      out_md[r] = hot_phys;
+      tags[slot] = (int32_t)jhost[j];
     }
-    for (int64_t i = total + tid; i < K; i += nthreads) out_mh[i] = out_md[i] = -1;
   }
-  if (tid < 3) out_counts[tid] = (int64_t)s_counts[tid];
+  for (int i = misses + tid; i < K; i += nthreads) out_mh[i] = out_md[i] = -1;
+  if (tid == 0) {
+    out_counts[0] = (int64_t)((totals >> (2 * kCountBits)) & kCountMask);
+    out_counts[1] = (int64_t)((totals >> kCountBits) & kCountMask);
+    out_counts[2] = misses;
+  }
   __syncthreads();
   // ---- 8. new LRU: stable partition by category of the old order ------------------
   {
-    const int64_t per = ceil_div(H, nthreads);
-    const int64_t lo = min(H, tid * per), hi = min(H, lo + per);
-    int64_t c01 = 0, c23 = 0;  // two 32-bit counters per 64-bit word
-    for (int64_t i = lo; i < hi; ++i) {
+    // four 16-bit counters (hot_rows <= 65535, checked on the host)
+    unsigned long long local = 0;
+    for (int i = hlo; i < hhi; ++i) {
       const uint8_t f = sflags[lru_old[i]];
       const int cat = ((f & kInserted) ? 1 : 0) + ((f & kProtected) ? 2 : 0);
-      if (cat < 2) c01 += (int64_t)1 << (32 * cat);
-      else c23 += (int64_t)1 << (32 * (cat - 2));
+      local += 1ull << (16 * cat);
     }
-    int64_t t01, t23;
-    const int64_t e01 = block_exclusive_scan<int64_t>(c01, scan_scratch, &t01);
-    const int64_t e23 = block_exclusive_scan<int64_t>(c23, scan_scratch, &t23);
-    const int64_t tot0 = t01 & 0xffffffff, tot1 = t01 >> 32, tot2 = t23 & 0xffffffff;
-    int64_t pos[4] = {e01 & 0xffffffff, tot0 + (e01 >> 32), tot0 + tot1 + (e23 & 0xffffffff),
-                      tot0 + tot1 + tot2 + (e23 >> 32)};
-    for (int64_t i = lo; i < hi; ++i) {
+    unsigned long long tot;
+    const unsigned long long e = block_exclusive_scan<unsigned long long>(local, scan_scratch, &tot);
+    const int t0 = (int)(tot & 0xffff), t1 = (int)((tot >> 16) & 0xffff),
+              t2 = (int)((tot >> 32) & 0xffff);
+    int pos[4] = {(int)(e & 0xffff), t0 + (int)((e >> 16) & 0xffff),
+                  t0 + t1 + (int)((e >> 32) & 0xffff), t0 + t1 + t2 + (int)((e >> 48) & 0xffff)};
+    for (int i = hlo; i < hhi; ++i) {
       const int32_t s = lru_old[i];
       const uint8_t f = sflags[s];
       const int cat = ((f & kInserted) ? 1 : 0) + ((f & kProtected) ? 2 : 0);
@@ -382,16 +307,110 @@ __global__ void __launch_bounds__(kResolveThreads) resolve_kernel(ResolveParams 
     }
   }
   // ---- 9. results in input order ------------------------------------------------------
-  for (int64_t i = tid; i < K; i += nthreads) {
-    const int64_t raw = load_position(p, b, i);
-    int64_t r = -1;
-    if (raw >= 0 && raw < length) {
-      const int64_t f = lower_bound(keys, K, raw);
-      if (first_in[f] == (int32_t)i) r = jphys[f];
+  if (sorted) {
+    // input order is sorted order: the first occurrence is the unique entry
+    for (int i = tid; i < K; i += nthreads) {
+      const bool first = keys[i] < length && (i == 0 || keys[i - 1] != keys[i]);
+      out_phys[i] = first ? jphys[i] : -1;
     }
-    out_phys[i] = r;
+  } else {
+    for (int i = tid; i < K; i += nthreads) {
+      const int64_t raw = load_position(p, b, i);
+      int64_t r = -1;
+      if (raw >= 0 && raw < length) {
+        const int f = lower_bound(keys, K, raw);
+        if (first_in[f] == i) r = jphys[f];
+      }
+      out_phys[i] = r;
+    }
   }
-head_columns:
+}
+
+
+__global__ void __launch_bounds__(kResolveThreads) resolve_kernel(ResolveParams p) {
+  extern __shared__ __align__(16) char smem_raw[];
+  __shared__ unsigned long long scan_scratch[33];
+  __shared__ int s_abort;
+  const int b = blockIdx.x;
+  const int tid = threadIdx.x, nthreads = blockDim.x;
+  const Layout L(p.count, p.hot_rows);
+  const int K = (int)p.count, H = (int)p.hot_rows, KP = (int)L.kp, CH = (int)L.ch;
+  char *base = p.workspace ? p.workspace + (size_t)b * L.total : smem_raw;
+  int32_t *keys = reinterpret_cast<int32_t *>(base + L.keys);
+  int32_t *first_in = reinterpret_cast<int32_t *>(base + L.first);
+  uint8_t *jflags = reinterpret_cast<uint8_t *>(base + L.flags);
+  int32_t *jslot = reinterpret_cast<int32_t *>(base + L.slot);
+  int32_t *jrank = reinterpret_cast<int32_t *>(base + L.rank);
+  int64_t *jhost = reinterpret_cast<int64_t *>(base + L.host);
+  int64_t *jphys = reinterpret_cast<int64_t *>(base + L.phys);
+  unsigned long long *table = reinterpret_cast<unsigned long long *>(base + L.hash);
+  uint8_t *sflags = reinterpret_cast<uint8_t *>(base + L.sflags);
+  int32_t *lru_old = reinterpret_cast<int32_t *>(base + L.lru_old);
+  int32_t *victims = reinterpret_cast<int32_t *>(base + L.victims);
+
+  int64_t *lru = p.lru.at(b);
+  const int64_t length = p.lengths.at(b);
+  int64_t *out_phys = p.out_physical + (int64_t)b * K;
+  int64_t *out_mh = p.out_miss_host + (int64_t)b * K;
+  int64_t *out_md = p.out_miss_device + (int64_t)b * K;
+  int64_t *out_counts = p.out_counts + (int64_t)b * 3;
+
+  if (tid == 0) s_abort = 0;
+  // ---- 1. normalise positions; clear the hash; copy the LRU ---------------------
+  for (int i = tid; i < KP; i += nthreads) {
+    int32_t v = INT32_MAX;
+    if (i < K) {
+      const int64_t raw = load_position(p, b, i);
+      v = (int32_t)((raw >= 0 && raw < length) ? raw : length);
+    }
+    keys[i] = v;
+  }
+  for (int s = tid; s < CH; s += nthreads) table[s] = kEmpty;
+  __syncthreads();
+  int unsorted = 0;
+  for (int i = tid; i + 1 < KP; i += nthreads) unsorted |= keys[i] > keys[i + 1];
+  for (int s = tid; s < H; s += nthreads) {
+    sflags[s] = 0;
+    const int64_t v = lru[s];
+    if (v < 0 || v >= H) s_abort = 1;
+    lru_old[s] = (int32_t)v;
+  }
+  // ---- 2. sort (skipped for sorted input such as Quest's, whose -1 padding
+  //         normalises past the end); first occurrence in input order --------
+  const bool sorted = !__syncthreads_or(unsorted);
+  if (!sorted) {
+    for (int i = tid; i < K; i += nthreads) first_in[i] = K;
+    for (int k = 2; k <= KP; k <<= 1) {
+      for (int j = k >> 1; j > 0; j >>= 1) {
+        for (int i = tid; i < KP; i += nthreads) {
+          const int l = i ^ j;
+          if (l > i) {
+            const int32_t a = keys[i], c = keys[l];
+            const bool up = (i & k) == 0;
+            if ((a > c) == up) {
+              keys[i] = c;
+              keys[l] = a;
+            }
+          }
+        }
+        __syncthreads();
+      }
+    }
+    for (int i = tid; i < K; i += nthreads) {
+      const int64_t raw = load_position(p, b, i);
+      if (raw >= 0 && raw < length) atomicMin(&first_in[lower_bound(keys, K, raw)], i);
+    }
+  }
+  if (s_abort) {
+    // a corrupt LRU permutation cannot be resolved faithfully: tables stay
+    // untouched and the plan is empty
+    for (int i = tid; i < K; i += nthreads) out_phys[i] = out_mh[i] = out_md[i] = -1;
+    if (tid < 3) out_counts[tid] = 0;
+    if (tid == 0) flag(p.status, HS_DEV_LRU_CORRUPT);
+  } else {
+    resolve_body(p, L, b, sorted, keys, first_in, jflags, jslot, jrank, jhost, jphys, table,
+                 sflags, lru_old, victims, scan_scratch);
+  }
   if (p.head_columns != nullptr) {
     __syncthreads();
     const int64_t n = p.head_count * p.head_width;
@@ -405,8 +424,10 @@ head_columns:
 int resolve_common(ResolveParams &p, size_t workspace_bytes, cudaStream_t stream) {
   if (p.batch < 1 || p.count < 1 || p.hot_rows < 1 || p.page_size < 1 || p.table_pages < 1)
     return set_error(HS_ERR_INVALID_ARGUMENT, "resolve: dimensions must be positive");
-  if (p.count > INT32_MAX || p.hot_rows > INT32_MAX)
-    return set_error(HS_ERR_INVALID_ARGUMENT, "resolve: count and hot_rows must fit int32");
+  if (p.count >= (1 << 21) || p.hot_rows > 65535)
+    return set_error(HS_ERR_UNSUPPORTED,
+                     "resolve: count must be < 2^21 and hot_rows <= 65535 (hot_rows is at "
+                     "most 32768 in a cache)");
   if (p.hot_blocks * (int64_t)p.page_size < p.hot_rows)
     return set_error(HS_ERR_INVALID_ARGUMENT,
                      "resolve: hot table of %lld blocks cannot address %lld hot rows",

@@ -24,6 +24,8 @@ DEVICE_FLAGS = {
     2: "ceil(length / page_size) exceeded the table capacity",
     4: "an LRU entry outside [0, hot_rows) was found; tables left unchanged",
     8: "more misses than hot rows; tables left unchanged",
+    16: "a bounded wait for an asynchronous copy ran out; results are invalid",
+    32: "a batched metadata pointer was not 16-byte aligned; the request was skipped",
 }
 
 _DTYPES = {torch.float32: HS_FLOAT32, torch.float16: HS_FLOAT16, torch.bfloat16: HS_BFLOAT16}
@@ -135,8 +137,10 @@ def device_flags(device, reset=True) -> list[str]:
     return [text for bit, text in DEVICE_FLAGS.items() if value & bit]
 
 
-def workspace(nbytes: int, device) -> torch.Tensor | None:
+def workspace(nbytes: int, device, zeroed: bool = False) -> torch.Tensor | None:
     """Scratch from the caching allocator (stream-ordered, graph-safe)."""
     if nbytes == 0:
         return None
+    if zeroed:
+        return torch.zeros(nbytes, dtype=torch.uint8, device=device)
     return torch.empty(nbytes, dtype=torch.uint8, device=device)

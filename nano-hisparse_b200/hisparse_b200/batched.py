@@ -70,7 +70,7 @@ class DecodeBatch:
         self.miss_host = torch.empty((b, self.width), dtype=torch.int64, device=dev)
         self.miss_device = torch.empty((b, self.width), dtype=torch.int64, device=dev)
         self.quest_ws_bytes = lib.hs_quest_workspace_bytes(b, self.max_pages)
-        self.quest_ws = _lib.workspace(self.quest_ws_bytes, dev)
+        self.quest_ws = _lib.workspace(self.quest_ws_bytes, dev, zeroed=True)
         self.resolve_ws_bytes = lib.hs_resolve_workspace_bytes(b, self.width, self.hot_rows)
         self.resolve_ws = _lib.workspace(self.resolve_ws_bytes, dev)
         self.attend_ws_bytes = lib.hs_attend_workspace_bytes(b, q_heads, cfg.kv_heads,

@@ -146,7 +146,7 @@ def quest_selection(query, minimum, maximum, length, page_size, top_pages, keep_
     tokens = torch.empty(width, dtype=torch.int32, device=device)
     counter = torch.empty(1, dtype=torch.int32, device=device)
     nbytes = lib.hs_quest_workspace_bytes(1, minimum.shape[0])
-    ws = _lib.workspace(nbytes, device)
+    ws = _lib.workspace(nbytes, device, zeroed=True)
     _lib.check(lib.hs_quest_select(
         query.data_ptr(), _lib.dtype_code(query.dtype), minimum.data_ptr(), maximum.data_ptr(),
         _lib.dtype_code(minimum.dtype), query.shape[0], minimum.shape[1], query.shape[1],

@@ -58,7 +58,7 @@ def test_host_side_validation_needs_no_device():
 
 def test_workspace_sizes():
     lib = _lib.load()
-    assert lib.hs_quest_workspace_bytes(2, 100) == 800
+    assert lib.hs_quest_workspace_bytes(2, 100) == 2 * 100 * 4 + 2 * 4  # scores + counters
     assert lib.hs_resolve_workspace_bytes(1, 2048, 4096) == 0  # fits shared memory
     assert lib.hs_resolve_workspace_bytes(2, 32768, 32768) > 2 * 1024 * 1024
     assert lib.hs_attend_workspace_bytes(16, 32, 8, 128, 2048) > 0

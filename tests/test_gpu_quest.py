@@ -120,7 +120,7 @@ def test_batched_matches_single():
     xptr = torch.tensor([t.data_ptr() for t in maxs], dtype=torch.int64, device=DEV)
     lens = torch.tensor(lengths, dtype=torch.int32, device=DEV)
     nbytes = lib.hs_quest_workspace_bytes(b, 300)
-    ws = torch.empty(nbytes, dtype=torch.uint8, device=DEV)
+    ws = torch.zeros(nbytes, dtype=torch.uint8, device=DEV)
     _lib.check(lib.hs_quest_select_batched(
         b, query.data_ptr(), hq * d, _lib.HS_BFLOAT16, mptr.data_ptr(), xptr.data_ptr(),
         _lib.HS_BFLOAT16, lens.data_ptr(), hq, hkv, d, 300, p, top, 1, tokens.data_ptr(), width,
