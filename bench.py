@@ -40,6 +40,7 @@ TOP_PAGES = 2048 // PAGE          # Quest budget of 2048 tokens incl. sink and t
 HOT_ROWS = 2 * 2048               # reference default: 2 x max_union_rows
 RESIDENT_FRACTION = 0.25
 DTYPE = torch.bfloat16
+MICRO = 2  # request groups pipelined on separate streams
 
 
 def workload_config():
@@ -56,6 +57,7 @@ def workload_config():
         "kv": "N(0,1) bf16, page min/max metadata from K (seed 1)",
         "l2": "inputs larger than L2 (about 12 GiB of metadata and KV rows read per step)",
         "parallelism": "requests sharded over ranks, no collective on the hot path",
+        "microbatches": MICRO,
     }
 
 
@@ -85,7 +87,7 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}",
-                 "--format=csv,noheader,nounits", "-lms", "200"],
+                 "--format=csv,noheader,nounits", "-lms", "50"],
                 stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
         except OSError:
             self.proc = None
@@ -162,8 +164,24 @@ def build_workload(device, seed, log):
             cache.add_layer(r, layer, CONTEXT, np.arange(base, base + n), resident, hot_list)
     torch.cuda.synchronize(device)
     log(f"generated KV, metadata and placement in {time.time() - t0:.1f}s")
-    batch = DecodeBatch(cache, list(range(REQUESTS)), LAYERS, mins, maxs, TOP_PAGES, Q_HEADS)
-    return cache, batch
+    return cache, mins, maxs
+
+
+def make_batches(cache, mins, maxs, micro, device):
+    """`micro` decode batches over disjoint request groups, each with its own
+    compute and transfer streams (micro-batch pipelining)."""
+    from hisparse_b200 import DecodeBatch
+
+    groups = [list(range(REQUESTS))[i::micro] for i in range(micro)]
+    batches = []
+    for g in groups:
+        streams = (torch.cuda.Stream(device=device), torch.cuda.Stream(device=device))
+        with torch.cuda.stream(streams[0]):
+            batches.append(DecodeBatch(cache, g, LAYERS, {r: mins[r] for r in g},
+                                       {r: maxs[r] for r in g}, TOP_PAGES, Q_HEADS,
+                                       streams=streams))
+    torch.cuda.synchronize(device)
+    return groups, batches
 
 
 def bytes_per_unit(valid_rows, misses):
@@ -200,13 +218,13 @@ def run_gpu(args, rank, world, local_rank, log):
     torch.cuda.set_device(device)
     hbm_peak, hbm_source = measured_peaks()
     link_peak = hostlink_peak(device)
-    cache, batch = build_workload(device, 1 + rank, log)
+    cache, mins, maxs = build_workload(device, 1 + rank, log)
+    groups, batches = make_batches(cache, mins, maxs, args.microbatches, device)
     steps, warmup = args.steps, args.warmup
     gen = torch.Generator(device=device).manual_seed(1000 + rank)
     total = steps + warmup
     queries = torch.randn((total, LAYERS, REQUESTS, Q_HEADS, HEAD_DIM), generator=gen,
                           device=device, dtype=torch.float32).to(DTYPE)
-    outs = torch.empty((LAYERS, REQUESTS, Q_HEADS, HEAD_DIM), dtype=DTYPE, device=device)
     counts = torch.zeros((total, LAYERS, REQUESTS, 3), dtype=torch.int64, device=device)
     compute = cache.compute
 
@@ -222,71 +240,128 @@ def run_gpu(args, rank, world, local_rank, log):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
-    for s in range(warmup):
-        for layer in range(LAYERS):
-            batch.layer(layer, queries[s, layer], outs[layer], counts[s, layer])
+    from hisparse_b200.batched import DecodeGraph
+
+    gq = [queries[:, :, g].contiguous() for g in groups]          # [total, L, Bg, Hq, D]
+    graph = DecodeGraph(batches, LAYERS)
+    log("captured one decode step as a CUDA graph")
+
+    def run_steps(first, last):
+        for s in range(first, last):
+            for i in range(len(groups)):
+                graph.queries[i].copy_(gq[i][s % total])
+            graph.replay()
+            for i, g in enumerate(groups):
+                counts[s % total, :, g] = graph.counts[i]
+
+    run_steps(0, warmup)
     barrier()
+    # ---- timed region: K steps, device-resident inputs ------------------------------
     sampler = ClockSampler(local_rank)
     sampler.start()
-    timing = []
     start = torch.cuda.Event(enable_timing=True)
     end = torch.cuda.Event(enable_timing=True)
     start.record(compute)
-    for s in range(warmup, total):
-        for layer in range(LAYERS):
-            batch.layer(layer, queries[s, layer], outs[layer], counts[s, layer], timing)
+    run_steps(warmup, total)
     end.record(compute)
     barrier()
     clocks = sampler.stop()
     elapsed_ms = max_over_ranks(start.elapsed_time(end))
-
-    # per-kernel device time over the timed region (events on each launch's stream)
-    per_kernel = {}
-    for name, a, b in timing:
-        per_kernel.setdefault(name, []).append(a.elapsed_time(b))
-    kernel_ms = {k: float(np.sum(v)) for k, v in per_kernel.items()}
-    launches = {k: len(v) for k, v in per_kernel.items()}
     timed_counts = counts[warmup:].cpu().numpy()  # [steps, L, B, 3]
+
+    # ---- per-stage device time: the same steps run eagerly with CUDA events on
+    # each launch's stream; a spin kernel ahead of every layer keeps the streams
+    # busy while the host enqueues, so no host gap lands inside a measured span
+    timing = []
+    eager_counts = [torch.zeros((steps, LAYERS, len(g), 3), dtype=torch.int64, device=device)
+                    for g in groups]
+    ref = torch.cuda.Event(enable_timing=True)
+    ref.record(compute)
+    for bt in batches:
+        bt.compute.wait_event(ref)
+    for s in range(warmup, total):
+        for layer in range(LAYERS):
+            for i, bt in enumerate(batches):
+                with torch.cuda.stream(bt.compute):
+                    torch.cuda._sleep(1_000_000)
+                    bt.layer(layer, gq[i][s, layer], graph.outputs[i][layer],
+                             eager_counts[i][s - warmup, layer], timing)
+    for bt in batches:
+        done = torch.cuda.Event()
+        done.record(bt.compute)
+        compute.wait_event(done)
+    ref_end = torch.cuda.Event(enable_timing=True)
+    ref_end.record(compute)
+    barrier()
+    for bt in batches:  # the eager pass leaves events the graph must not wait on
+        for st in bt.layers:
+            st.ready = st.last_use = None
+    intervals = {}
+    for name, a, b in timing:
+        intervals.setdefault(name, []).append((ref.elapsed_time(a), ref.elapsed_time(b)))
+    kernel_ms = {k: float(sum(e - s_ for s_, e in v)) for k, v in intervals.items()}
+    launches = {k: len(v) for k, v in intervals.items()}
+
+    def union_ms(spans):
+        spans, total_ms, cur_s, cur_e = sorted(spans), 0.0, None, None
+        for s_, e in spans:
+            if cur_e is None or s_ > cur_e:
+                if cur_e is not None:
+                    total_ms += cur_e - cur_s
+                cur_s, cur_e = s_, e
+            else:
+                cur_e = max(cur_e, e)
+        return total_ms + ((cur_e - cur_s) if cur_e is not None else 0.0)
+
+    gather_busy_ms = union_ms(intervals["gather"])
     misses = int(timed_counts[..., 2].sum())
-    valid_rows = int(timed_counts.sum())
     row_bytes = 2 * KV_HEADS * HEAD_DIM * 2
     gather_bytes = misses * row_bytes
-    gather_gbs = gather_bytes / (kernel_ms["gather"] * 1e-3) / 1e9
+    # the eager pass repeats the timed steps' queries, but the hot buffer has
+    # moved on: its own miss bytes come from its own resolver counts
+    eager = np.concatenate([c.cpu().numpy() for c in eager_counts], axis=2)
+    eager_gather_bytes = int(eager[..., 2].sum()) * row_bytes
+    # micro-batches' gathers overlap on the one host link: the link's rate is
+    # the bytes over the time any gather is running
+    gather_gbs = eager_gather_bytes / (gather_busy_ms * 1e-3) / 1e9
     hbm_bytes = sum(bytes_per_unit(int(timed_counts[s, l, b].sum()), int(timed_counts[s, l, b, 2]))
                     for s in range(steps) for l in range(LAYERS) for b in range(REQUESTS))
-    attend_bytes = valid_rows * row_bytes
-    attend_gbs = attend_bytes / (kernel_ms["attend"] * 1e-3) / 1e9
+    attend_ms = kernel_ms["attend_ready"] + kernel_ms["attend_gathered"]
+    attend_bytes = int(eager.sum()) * row_bytes
+    attend_gbs = attend_bytes / (attend_ms * 1e-3) / 1e9
     meta_bytes = steps * LAYERS * REQUESTS * 2 * math.ceil(CONTEXT / PAGE) * KV_HEADS * \
         HEAD_DIM * 2
     quest_gbs = meta_bytes / (kernel_ms["quest"] * 1e-3) / 1e9
     t_roof = max(hbm_bytes / (hbm_peak * 1e9), gather_bytes / (link_peak * 1e9))
     step_frac = t_roof / (elapsed_ms * 1e-3)
 
-    # ---- end to end through the public API with host buffers ------------------------
-    host_q = queries.cpu().pin_memory()
-    host_out = torch.empty((total, LAYERS, REQUESTS, Q_HEADS, HEAD_DIM), dtype=DTYPE,
-                           pin_memory=True)
-    dev_q = torch.empty((LAYERS, REQUESTS, Q_HEADS, HEAD_DIM), dtype=DTYPE, device=device)
-    for s in range(warmup):
-        for layer in range(LAYERS):
-            dev_q[layer].copy_(host_q[s, layer], non_blocking=True)
-            batch.layer(layer, dev_q[layer], outs[layer])
-            host_out[s, layer].copy_(outs[layer], non_blocking=True)
+    # ---- end to end: queries copied in from pinned host memory and outputs read
+    # back every step, through the same captured step ------------------------------
+    host_q = [g.cpu().pin_memory() for g in gq]
+    host_out = [torch.empty((total, *o.shape), dtype=DTYPE, pin_memory=True)
+                for o in graph.outputs]
+
+    def run_e2e(first, last):
+        for s in range(first, last):
+            for i in range(len(groups)):
+                graph.queries[i].copy_(host_q[i][s % total], non_blocking=True)
+            graph.replay()
+            for i in range(len(groups)):
+                host_out[i][s % total].copy_(graph.outputs[i], non_blocking=True)
+
+    run_e2e(0, warmup)
     barrier()
     e2e_start = torch.cuda.Event(enable_timing=True)
     e2e_end = torch.cuda.Event(enable_timing=True)
     e2e_start.record(compute)
-    for s in range(warmup, total):
-        for layer in range(LAYERS):
-            dev_q[layer].copy_(host_q[s, layer], non_blocking=True)
-            batch.layer(layer, dev_q[layer], outs[layer])
-            host_out[s, layer].copy_(outs[layer], non_blocking=True)
+    run_e2e(warmup, total)
     e2e_end.record(compute)
     barrier()
     e2e_ms = max_over_ranks(e2e_start.elapsed_time(e2e_end))
     flags = _lib.device_flags(device)
     if flags:
         raise RuntimeError(f"device flags raised during the bench: {flags}")
+    prof_ms = ref.elapsed_time(ref_end)
 
     tokens = REQUESTS * steps * world
     value = tokens / (elapsed_ms * 1e-3)
@@ -298,21 +373,28 @@ def run_gpu(args, rank, world, local_rank, log):
         "data": "synthetic", "config": workload_config(),
         "e2e": {"value": round(tokens / (e2e_ms * 1e-3), 2), "unit": "tok/s",
                 "h2d_bytes_per_step": io_bytes, "d2h_bytes_per_step": io_bytes},
-        "gpu_launches": int(sum(launches.values()) + launches["quest"] + launches["attend"]),
+        # per layer and micro-batch: quest, resolve, gather, two attention phases
+        # and the merge (replayed from one CUDA graph per step)
+        "gpu_launches": int(6 * LAYERS * steps * len(batches)),
         "roofline": {
             "kernel": "gather_kernel (host->pool miss gather)", "bound": "hostlink",
             "achieved": round(gather_gbs, 2),
             "peak": round(link_peak, 2), "unit": "GB/s", "frac": round(gather_gbs / link_peak, 4),
             "peak_source": "measured in bench.py: pinned host->device cudaMemcpyAsync, 1 GiB",
             "traffic": None,
-            "bytes_per_launch": round(gather_bytes / launches["gather"]),
+            "achieved_definition": "miss bytes / time any gather launch is running (CUDA events "
+                                   "on the transfer streams; the micro-batches' gathers share "
+                                   "the link)",
+            "bytes_per_launch": round(eager_gather_bytes / launches["gather"]),
             "ms_per_launch": round(kernel_ms["gather"] / launches["gather"], 4),
+            "hostlink_busy_frac_eager": round(gather_busy_ms / prof_ms, 4),
         },
         "roofline_hbm": {
-            "attend_kernel": {"achieved": round(attend_gbs, 1), "peak": hbm_peak,
-                              "frac": round(attend_gbs / hbm_peak, 4), "unit": "GB/s",
-                              "peak_source": hbm_source,
-                              "ms_per_launch": round(kernel_ms["attend"] / launches["attend"], 4)},
+            "attend_kernels": {"achieved": round(attend_gbs, 1), "peak": hbm_peak,
+                               "frac": round(attend_gbs / hbm_peak, 4), "unit": "GB/s",
+                               "peak_source": hbm_source,
+                               "note": "ready-row phase runs concurrently with the gather",
+                               "ms_per_launch": round(attend_ms / launches["attend_ready"], 4)},
             "quest_kernels": {"achieved": round(quest_gbs, 1), "peak": hbm_peak,
                               "frac": round(quest_gbs / hbm_peak, 4), "unit": "GB/s",
                               "peak_source": hbm_source,
@@ -328,6 +410,7 @@ def run_gpu(args, rank, world, local_rank, log):
                      "hot_hits": int(timed_counts[..., 1].sum()), "misses": misses,
                      "miss_rows_per_unit": round(misses / (steps * LAYERS * REQUESTS), 1)},
         "kernel_ms_per_step": {k: round(v / steps, 3) for k, v in kernel_ms.items()},
+        "kernel_ms_note": "sums of launch durations over all micro-batches; launches overlap",
         "clocks": clocks,
     }
     return result
@@ -405,19 +488,21 @@ def cpu_sample(seed=1, budget_s=10.0, threads=None, log=print):
 
 
 def main():
-    global REQUESTS, LAYERS
+    global REQUESTS, LAYERS, MICRO
     parser = argparse.ArgumentParser(description=__doc__.split("\n\n")[0])
     parser.add_argument("--gpus", type=int, default=1)
     parser.add_argument("--steps", type=int, default=10)
     parser.add_argument("--warmup", type=int, default=3)
     parser.add_argument("--impl", default="hisparse_b200", choices=["hisparse_b200", "reference"])
     parser.add_argument("--no-cpu-baseline", action="store_true")
+    parser.add_argument("--microbatches", type=int, default=2,
+                        help="independent request groups pipelined on separate streams")
     # Smaller request/layer counts are for ncu captures only; the bench line of
     # configuration 2 uses the defaults.
     parser.add_argument("--requests", type=int, default=REQUESTS)
     parser.add_argument("--layers", type=int, default=LAYERS)
     args = parser.parse_args()
-    REQUESTS, LAYERS = args.requests, args.layers
+    REQUESTS, LAYERS, MICRO = args.requests, args.layers, args.microbatches
     rank = int(os.environ.get("RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", 1))
     local_rank = int(os.environ.get("LOCAL_RANK", 0))

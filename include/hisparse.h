@@ -177,7 +177,11 @@ HS_API int hs_resolve_rows(const void *positions, int positions_dtype, int64_t c
 /* Batched: positions int32 [batch, count]; per-request tables as device
  * pointer arrays; lengths device int32[batch]; outputs [batch, count] and
  * out_counts [batch, 3]. table_pages is a capacity every request's
- * source/resident tables satisfy. */
+ * source/resident tables satisfy. out_ready (optional, [batch, count]) receives
+ * the physical rows that need no gather (resident and hot hits), compact in
+ * sorted logical order and -1 padded: out_counts[b][0] + out_counts[b][1] of
+ * them; with miss_device (out_counts[b][2] rows) it lets attention over the
+ * ready rows run while the misses are gathered. */
 HS_API int hs_resolve_rows_batched(int batch, const int32_t *positions, int64_t count,
                             const uint64_t *source_ptrs, const uint64_t *resident_ptrs,
                             int64_t table_pages, const uint64_t *hot_ptrs,
@@ -185,8 +189,9 @@ HS_API int hs_resolve_rows_batched(int batch, const int32_t *positions, int64_t 
                             const uint64_t *lru_ptrs, int64_t hot_rows,
                             const int32_t *lengths, int page_size, int64_t *out_physical,
                             int64_t *out_miss_host, int64_t *out_miss_device,
-                            int64_t *out_counts, void *workspace, size_t workspace_bytes,
-                            int32_t *device_status, hs_stream stream);
+                            int64_t *out_counts, int64_t *out_ready, void *workspace,
+                            size_t workspace_bytes, int32_t *device_status,
+                            hs_stream stream);
 
 /* ---- (3) miss gather --------------------------------------------------------
  * Replaces gather_rows (nano_hisparse/row_kernels.py:35-70): for every i with
@@ -223,6 +228,30 @@ HS_API int hs_attend_rows(int batch, const void *query, int64_t query_batch_stri
                    int64_t out_batch_stride, int q_heads, int kv_heads, int head_dim,
                    int page_size, void *workspace, size_t workspace_bytes,
                    int32_t *device_status, hs_stream stream);
+
+/* Two-phase form, for overlapping attention with the miss gather. A phase
+ * launch attends over the leading valid rows of `rows` ([batch, count],
+ * shared by all heads of a request) and leaves (max, sum, O) partials in the
+ * workspace under `phase` (0 or 1); hs_attend_merge combines phases 0..phases-1
+ * into `out`. The valid rows of batch item b are its first
+ * sum(valid_counts[b*counts_stride + counts_first + i], i < counts_n) entries
+ * (all `count` when valid_counts is NULL) — e.g. the resolver's counts select
+ * the ready list (components 0-1) and the miss plan (component 2). Both calls
+ * use the workspace sized by hs_attend_workspace_bytes for the same arguments
+ * and must run in stream order. */
+HS_API int hs_attend_rows_phase(int batch, const void *query, int64_t query_batch_stride,
+                                int query_dtype, const void *pool, int64_t pool_blocks,
+                                int kv_dtype, const int64_t *rows, int64_t rows_batch_stride,
+                                int64_t count, const int64_t *valid_counts, int counts_stride,
+                                int counts_first, int counts_n, int phase, int q_heads,
+                                int kv_heads, int head_dim, int page_size, void *workspace,
+                                size_t workspace_bytes, int32_t *device_status,
+                                hs_stream stream);
+
+HS_API int hs_attend_merge(int batch, int phases, void *out, int64_t out_batch_stride,
+                           int query_dtype, int q_heads, int kv_heads, int head_dim,
+                           int64_t count, void *workspace, size_t workspace_bytes,
+                           int32_t *device_status, hs_stream stream);
 
 #ifdef __cplusplus
 }

@@ -3,6 +3,7 @@
 #include <atomic>
 #include <cstdarg>
 #include <cstdio>
+#include <mutex>
 
 #include "common.cuh"
 
@@ -39,6 +40,35 @@ int sm_count() {
     g_sm_count[dev].store(n, std::memory_order_relaxed);
   }
   return n;
+}
+
+int reserve_smem(const void *func, size_t bytes, const char *what) {
+  if (bytes <= 48 * 1024) return HS_OK;
+  struct Entry {
+    const void *func;
+    int device;
+    size_t bytes;
+  };
+  static std::mutex lock;
+  static Entry table[256];
+  static int used = 0;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::lock_guard<std::mutex> guard(lock);
+  for (int i = 0; i < used; ++i)
+    if (table[i].func == func && table[i].device == dev && table[i].bytes >= bytes) return HS_OK;
+  if (cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes) !=
+      cudaSuccess) {
+    cudaGetLastError();
+    return set_error(HS_ERR_CUDA, "%s: cannot reserve %zu bytes of shared memory", what, bytes);
+  }
+  for (int i = 0; i < used; ++i)
+    if (table[i].func == func && table[i].device == dev) {
+      table[i].bytes = bytes;
+      return HS_OK;
+    }
+  if (used < 256) table[used++] = Entry{func, dev, bytes};
+  return HS_OK;
 }
 
 }  // namespace hs

@@ -36,9 +36,36 @@ struct AttendParams {
   int splits, head_chunks;  // grid.y = kv_heads * head_chunks (shared) or q_heads (per head)
   int page_shift;           // log2(page_size) when a power of two, else -1
   float scale;
-  float *partials;  // [batch, q_heads, splits, head_dim + 2]
+  float *partials;          // [2 phases][batch][q_heads][split_stride][head_dim + 2]
+  int split_stride;         // splits capacity of the workspace
+  int phase, phases;        // partial set written by a phase launch / merged by the merge
+  int *phase_splits;        // [2] splits each phase used (written by the phase launch)
+  const int64_t *valid_counts;  // optional: rows valid per batch item = sum of
+  int counts_stride, counts_first, counts_n;  // valid_counts[b*stride + first .. +n)
   int32_t *status;
 };
+
+// Leading rows of batch item b that a phase reads, and the [begin, end) part
+// of them split `split` covers (an even share of the valid rows).
+__device__ __forceinline__ void split_range(const AttendParams &p, int b, int split,
+                                            int64_t &begin, int64_t &end) {
+  int64_t valid = p.count;
+  if (p.valid_counts) {
+    valid = 0;
+    for (int i = 0; i < p.counts_n; ++i)
+      valid += p.valid_counts[(int64_t)b * p.counts_stride + p.counts_first + i];
+    valid = valid < 0 ? 0 : (valid > p.count ? p.count : valid);
+  }
+  const int64_t chunk = ceil_div(valid, p.splits);
+  begin = split * chunk;
+  end = min(valid, begin + chunk);
+}
+
+__device__ __forceinline__ float *partial_slot(const AttendParams &p, int b, int h, int split) {
+  return p.partials +
+         (((int64_t)(p.phase * p.batch + b) * p.q_heads + h) * p.split_stride + split) *
+             (p.head_dim + 2);
+}
 
 __host__ __device__ inline int attend_splits(int batch, int kv_heads, int64_t count, int sms) {
   const int64_t target = (int64_t)sms * 8;
@@ -91,10 +118,12 @@ __global__ void __launch_bounds__(kAttendThreads) attend_split_kernel(AttendPara
     for (int c = 0; c < C; ++c) acc[g][c] = 0.f;
   }
 
-  const int64_t chunk = ceil_div(p.count, p.splits);
-  const int64_t begin = split * chunk, end = min(p.count, begin + chunk);
+  int64_t begin, end;
+  split_range(p, b, split, begin, end);
   const int64_t *rows = p.rows + (int64_t)b * p.rows_batch_stride +
                         (shared_rows ? 0 : (int64_t)h0 * p.rows_head_stride);
+  if (split == 0 && b == 0 && blockIdx.y == 0 && threadIdx.x == 0)
+    p.phase_splits[p.phase] = p.splits;
   const int64_t row_elems = (int64_t)p.kv_heads * D;
   const int64_t plane_elems = (int64_t)p.page_size * row_elems;
   const TKV *pool = reinterpret_cast<const TKV *>(p.pool);
@@ -179,7 +208,7 @@ __global__ void __launch_bounds__(kAttendThreads) attend_split_kernel(AttendPara
         v += f * (e == D + 1 ? red_l[w][g] : red_acc[w][g][e]);
       }
     }
-    p.partials[(((int64_t)b * p.q_heads + h0 + g) * p.splits + split) * stride + e] = v;
+    partial_slot(p, b, h0 + g, split)[e] = v;
   }
 }
 
@@ -279,8 +308,9 @@ __global__ void __launch_bounds__(kMmaThreads, 1) attend_mma_kernel(AttendParams
   const int kh = active ? warp / p.head_chunks : 0;
   const int h0 = kh * groups + (warp % p.head_chunks) * 16;
   const int hn = active ? min(16, kh * groups + groups - h0) : 0;
-  const int64_t chunk = ceil_div(p.count, p.splits);
-  const int64_t begin = split * chunk, end = min(p.count, begin + chunk);
+  int64_t begin, end;
+  split_range(p, b, split, begin, end);
+  if (split == 0 && b == 0 && tid == 0) p.phase_splits[p.phase] = p.splits;
   const int64_t *rows = p.rows + (int64_t)b * p.rows_batch_stride;
   const int64_t row_elems = (int64_t)p.kv_heads * 128;
   const int64_t plane = (int64_t)p.page_size * row_elems;
@@ -450,7 +480,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1) attend_mma_kernel(AttendParams
     l += __shfl_xor_sync(kFullMask, l, 2);
     const int m = (lane >> 2) + hh * 8;
     if (m >= hn) continue;
-    float *dst = p.partials + (((int64_t)b * p.q_heads + h0 + m) * p.splits + split) * stride;
+    float *dst = partial_slot(p, b, h0 + m, split);
     if ((lane & 3) == 0) {
       dst[128] = m_run[hh] * 0.6931471805599453f;  // log2 units -> natural log for the merge
       dst[129] = l;
@@ -468,20 +498,31 @@ template <typename TQ>
 __global__ void attend_merge_kernel(AttendParams p) {
   const int h = blockIdx.x, b = blockIdx.y;
   const int D = p.head_dim, stride = D + 2;
-  const float *part = p.partials + ((int64_t)b * p.q_heads + h) * p.splits * stride;
   float mm = -INFINITY;
-  for (int s = 0; s < p.splits; ++s) mm = fmaxf(mm, part[s * stride + D]);
+  for (int ph = 0; ph < p.phases; ++ph) {
+    p.phase = ph;
+    const int splits = p.phase_splits[ph];
+    for (int s = 0; s < splits; ++s) mm = fmaxf(mm, partial_slot(p, b, h, s)[D]);
+  }
   float denom = 0.f;
-  for (int s = 0; s < p.splits; ++s) {
-    const float ms = part[s * stride + D];
-    if (ms != -INFINITY) denom += expf(ms - mm) * part[s * stride + D + 1];
+  for (int ph = 0; ph < p.phases; ++ph) {
+    p.phase = ph;
+    const int splits = p.phase_splits[ph];
+    for (int s = 0; s < splits; ++s) {
+      const float *part = partial_slot(p, b, h, s);
+      if (part[D] != -INFINITY) denom += expf(part[D] - mm) * part[D + 1];
+    }
   }
   TQ *out = static_cast<TQ *>(p.out) + (int64_t)b * p.out_batch_stride + (int64_t)h * D;
   for (int d = threadIdx.x; d < D; d += blockDim.x) {
     float num = 0.f;
-    for (int s = 0; s < p.splits; ++s) {
-      const float ms = part[s * stride + D];
-      if (ms != -INFINITY) num += expf(ms - mm) * part[s * stride + d];
+    for (int ph = 0; ph < p.phases; ++ph) {
+      p.phase = ph;
+      const int splits = p.phase_splits[ph];
+      for (int s = 0; s < splits; ++s) {
+        const float *part = partial_slot(p, b, h, s);
+        if (part[D] != -INFINITY) num += expf(part[D] - mm) * part[d];
+      }
     }
     out[d] = from_f32<TQ>(denom > 0.f ? num / denom : 0.f);
   }
@@ -514,16 +555,11 @@ int launch(AttendParams &p, cudaStream_t stream) {
       const MmaShape sh = mma_shape(p.kv_heads);
       const int kMmaSmem = kStages * sh.stage_bytes;
       p.splits = mma_splits(p.batch, p.count, sh.stage_rows, sm_count());
-      if (cudaFuncSetAttribute(attend_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               kMmaSmem) != cudaSuccess)
-        return set_error(HS_ERR_CUDA, "attend: cannot reserve %d bytes of shared memory",
-                         kMmaSmem);
+      const int rc = reserve_smem((const void *)attend_mma_kernel, kMmaSmem, "attend");
+      if (rc != HS_OK) return rc;
       dim3 grid(p.splits, 1, p.batch);
       attend_mma_kernel<<<grid, kMmaThreads, kMmaSmem, stream>>>(p);
-      int rc = check_launch("attend_mma_kernel");
-      if (rc != HS_OK) return rc;
-      attend_merge_kernel<TQ><<<dim3(p.q_heads, p.batch), 128, 0, stream>>>(p);
-      return check_launch("attend_merge_kernel");
+      return check_launch("attend_mma_kernel");
     }
   }
   const int C = (p.head_dim + 31) / 32;
@@ -537,8 +573,10 @@ int launch(AttendParams &p, cudaStream_t stream) {
     case 4: attend_split_kernel<TQ, TKV, 4><<<grid, kAttendThreads, 0, stream>>>(p); break;
     default: attend_split_kernel<TQ, TKV, 8><<<grid, kAttendThreads, 0, stream>>>(p); break;
   }
-  int rc = check_launch("attend_split_kernel");
-  if (rc != HS_OK) return rc;
+  return check_launch("attend_split_kernel");
+}
+
+template <typename TQ> int launch_merge(AttendParams &p, cudaStream_t stream) {
   attend_merge_kernel<TQ><<<dim3(p.q_heads, p.batch), 128, 0, stream>>>(p);
   return check_launch("attend_merge_kernel");
 }
@@ -555,22 +593,25 @@ template <typename TQ> int dispatch_kv(int kv_dtype, AttendParams &p, cudaStream
 }  // namespace
 }  // namespace hs
 
-extern "C" size_t hs_attend_workspace_bytes(int batch, int q_heads, int kv_heads,
-                                            int head_dim, int64_t count) {
-  if (batch < 1 || q_heads < 1 || kv_heads < 1 || head_dim < 1 || count < 1) return 0;
-  const int splits = hs::max_splits(batch, kv_heads, count, hs::sm_count());
-  return (size_t)batch * q_heads * splits * (head_dim + 2) * sizeof(float);
-}
+namespace hs {
+namespace {
 
-extern "C" int hs_attend_rows(int batch, const void *query, int64_t query_batch_stride,
-                              int query_dtype, const void *pool, int64_t pool_blocks,
-                              int kv_dtype, const int64_t *rows, int64_t rows_batch_stride,
-                              int64_t rows_head_stride, int64_t count, void *out,
-                              int64_t out_batch_stride, int q_heads, int kv_heads,
-                              int head_dim, int page_size, void *workspace,
-                              size_t workspace_bytes, int32_t *device_status,
-                              hs_stream stream) {
-  using namespace hs;
+// Workspace: partials of two phases, then the splits each phase used.
+struct AttendWorkspace {
+  size_t partial_floats, bytes;
+  int split_stride;
+  AttendWorkspace(int batch, int q_heads, int kv_heads, int head_dim, int64_t count) {
+    split_stride = max_splits(batch, kv_heads, count, sm_count());
+    partial_floats = (size_t)2 * batch * q_heads * split_stride * (head_dim + 2);
+    bytes = partial_floats * sizeof(float) + 2 * sizeof(int);
+  }
+};
+
+int prepare(AttendParams &p, int batch, const void *query, int64_t query_batch_stride,
+            const void *pool, int64_t pool_blocks, const int64_t *rows,
+            int64_t rows_batch_stride, int64_t rows_head_stride, int64_t count, int q_heads,
+            int kv_heads, int head_dim, int page_size, void *workspace,
+            size_t workspace_bytes, int32_t *device_status) {
   if (batch < 1 || q_heads < 1 || kv_heads < 1 || head_dim < 1 || page_size < 1 ||
       count < 1 || pool_blocks < 0)
     return set_error(HS_ERR_INVALID_ARGUMENT, "attend: dimensions must be positive");
@@ -578,13 +619,13 @@ extern "C" int hs_attend_rows(int batch, const void *query, int64_t query_batch_
     return set_error(HS_ERR_INVALID_ARGUMENT, "query GQA/device mismatch");
   if (head_dim > 256)
     return set_error(HS_ERR_UNSUPPORTED, "attend: head_dim %d > 256 is not supported", head_dim);
-  if (!query || !pool || !rows || !out)
+  if (!query || !pool || !rows)
     return set_error(HS_ERR_INVALID_ARGUMENT, "attend: null tensor pointer");
-  const size_t need = hs_attend_workspace_bytes(batch, q_heads, kv_heads, head_dim, count);
-  if (!workspace || workspace_bytes < need)
+  const AttendWorkspace ws(batch, q_heads, kv_heads, head_dim, count);
+  if (!workspace || workspace_bytes < ws.bytes)
     return set_error(HS_ERR_WORKSPACE, "attend: workspace of %zu bytes < required %zu",
-                     workspace_bytes, need);
-  AttendParams p{};
+                     workspace_bytes, ws.bytes);
+  p = AttendParams{};
   p.batch = batch;
   p.query = query;
   p.query_batch_stride = query_batch_stride;
@@ -594,8 +635,6 @@ extern "C" int hs_attend_rows(int batch, const void *query, int64_t query_batch_
   p.rows_batch_stride = rows_batch_stride;
   p.rows_head_stride = rows_head_stride;
   p.count = count;
-  p.out = out;
-  p.out_batch_stride = out_batch_stride;
   p.q_heads = q_heads;
   p.kv_heads = kv_heads;
   p.head_dim = head_dim;
@@ -607,12 +646,107 @@ extern "C" int hs_attend_rows(int batch, const void *query, int64_t query_batch_
     for (int sh = 0; sh < 31; ++sh)
       if ((1 << sh) == page_size) p.page_shift = sh;
   p.partials = static_cast<float *>(workspace);
+  p.split_stride = ws.split_stride;
+  p.phase_splits = reinterpret_cast<int *>(static_cast<float *>(workspace) + ws.partial_floats);
   p.status = device_status;
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  return HS_OK;
+}
+
+int run_phase(AttendParams &p, int query_dtype, int kv_dtype, cudaStream_t s) {
   switch (query_dtype) {
     case HS_FLOAT32: return dispatch_kv<float>(kv_dtype, p, s);
     case HS_FLOAT16: return dispatch_kv<__half>(kv_dtype, p, s);
     case HS_BFLOAT16: return dispatch_kv<__nv_bfloat16>(kv_dtype, p, s);
   }
   return set_error(HS_ERR_INVALID_ARGUMENT, "attend: invalid query dtype %d", query_dtype);
+}
+
+int run_merge(AttendParams &p, int query_dtype, cudaStream_t s) {
+  switch (query_dtype) {
+    case HS_FLOAT32: return launch_merge<float>(p, s);
+    case HS_FLOAT16: return launch_merge<__half>(p, s);
+    case HS_BFLOAT16: return launch_merge<__nv_bfloat16>(p, s);
+  }
+  return set_error(HS_ERR_INVALID_ARGUMENT, "attend: invalid query dtype %d", query_dtype);
+}
+
+}  // namespace
+}  // namespace hs
+
+extern "C" size_t hs_attend_workspace_bytes(int batch, int q_heads, int kv_heads,
+                                            int head_dim, int64_t count) {
+  if (batch < 1 || q_heads < 1 || kv_heads < 1 || head_dim < 1 || count < 1) return 0;
+  return hs::AttendWorkspace(batch, q_heads, kv_heads, head_dim, count).bytes;
+}
+
+extern "C" int hs_attend_rows(int batch, const void *query, int64_t query_batch_stride,
+                              int query_dtype, const void *pool, int64_t pool_blocks,
+                              int kv_dtype, const int64_t *rows, int64_t rows_batch_stride,
+                              int64_t rows_head_stride, int64_t count, void *out,
+                              int64_t out_batch_stride, int q_heads, int kv_heads,
+                              int head_dim, int page_size, void *workspace,
+                              size_t workspace_bytes, int32_t *device_status,
+                              hs_stream stream) {
+  using namespace hs;
+  if (!out) return set_error(HS_ERR_INVALID_ARGUMENT, "attend: null tensor pointer");
+  AttendParams p;
+  int rc = prepare(p, batch, query, query_batch_stride, pool, pool_blocks, rows,
+                   rows_batch_stride, rows_head_stride, count, q_heads, kv_heads, head_dim,
+                   page_size, workspace, workspace_bytes, device_status);
+  if (rc != HS_OK) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  p.phase = 0;
+  rc = run_phase(p, query_dtype, kv_dtype, s);
+  if (rc != HS_OK) return rc;
+  p.phases = 1;
+  p.out = out;
+  p.out_batch_stride = out_batch_stride;
+  return run_merge(p, query_dtype, s);
+}
+
+extern "C" int hs_attend_rows_phase(int batch, const void *query, int64_t query_batch_stride,
+                                    int query_dtype, const void *pool, int64_t pool_blocks,
+                                    int kv_dtype, const int64_t *rows,
+                                    int64_t rows_batch_stride, int64_t count,
+                                    const int64_t *valid_counts, int counts_stride,
+                                    int counts_first, int counts_n, int phase, int q_heads,
+                                    int kv_heads, int head_dim, int page_size, void *workspace,
+                                    size_t workspace_bytes, int32_t *device_status,
+                                    hs_stream stream) {
+  using namespace hs;
+  if (phase != 0 && phase != 1)
+    return set_error(HS_ERR_INVALID_ARGUMENT, "attend: phase must be 0 or 1");
+  if (valid_counts && (counts_stride < 1 || counts_first < 0 || counts_n < 1))
+    return set_error(HS_ERR_INVALID_ARGUMENT, "attend: invalid count selector");
+  AttendParams p;
+  int rc = prepare(p, batch, query, query_batch_stride, pool, pool_blocks, rows,
+                   rows_batch_stride, 0, count, q_heads, kv_heads, head_dim, page_size,
+                   workspace, workspace_bytes, device_status);
+  if (rc != HS_OK) return rc;
+  p.phase = phase;
+  p.valid_counts = valid_counts;
+  p.counts_stride = counts_stride;
+  p.counts_first = counts_first;
+  p.counts_n = counts_n;
+  return run_phase(p, query_dtype, kv_dtype, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int hs_attend_merge(int batch, int phases, void *out, int64_t out_batch_stride,
+                               int query_dtype, int q_heads, int kv_heads, int head_dim,
+                               int64_t count, void *workspace, size_t workspace_bytes,
+                               int32_t *device_status, hs_stream stream) {
+  using namespace hs;
+  if (phases != 1 && phases != 2)
+    return set_error(HS_ERR_INVALID_ARGUMENT, "attend: phases must be 1 or 2");
+  if (!out) return set_error(HS_ERR_INVALID_ARGUMENT, "attend: null tensor pointer");
+  AttendParams p;
+  // the merge reads no rows or pool: any non-null placeholders pass validation
+  int rc = prepare(p, batch, out, 0, out, 0, reinterpret_cast<const int64_t *>(out), 0, 0,
+                   count, q_heads, kv_heads, head_dim, 1, workspace, workspace_bytes,
+                   device_status);
+  if (rc != HS_OK) return rc;
+  p.phases = phases;
+  p.out = out;
+  p.out_batch_stride = out_batch_stride;
+  return run_merge(p, query_dtype, static_cast<cudaStream_t>(stream));
 }

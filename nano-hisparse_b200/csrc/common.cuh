@@ -17,6 +17,10 @@ constexpr unsigned kFullMask = 0xffffffffu;
 int set_error(int status, const char *fmt, ...);
 int check_launch(const char *what);
 int sm_count();
+// Raises `func`'s dynamic shared-memory limit to at least `bytes` on the
+// current device, calling the runtime only the first time a larger limit is
+// needed (so launches inside a CUDA-graph capture make no such call).
+int reserve_smem(const void *func, size_t bytes, const char *what);
 
 // ---- element types ---------------------------------------------------------
 template <typename T> struct Elem;

@@ -5,15 +5,15 @@
 // Reference: nano_hisparse/row_kernels.py:35-70 (_gather, gather_rows) and the
 // CPU loop of hybrid.py:452-459. The reference runs min(n, 64) programs and
 // recompiles per plan width; here the plan width is a runtime argument and
-// the grid covers every SM. One warp moves one row: all 2*row_bytes of it are
-// loaded (16-byte vectors when the layout allows) before any store, so each
-// warp keeps up to 4 KiB of host-link reads in flight.
+// the grid has one 4-warp CTA per SM. One warp moves one row: all 2*row_bytes
+// of it are loaded (16-byte vectors when the layout allows) before any store,
+// so each warp keeps up to 4 KiB of host-link reads in flight.
 #include "common.cuh"
 
 namespace hs {
 namespace {
 
-constexpr int kGatherThreads = 256;
+constexpr int kGatherThreads = 128;
 constexpr int kGatherWarps = kGatherThreads / 32;
 constexpr int kUnroll = 8;  // vectors per lane in flight
 
@@ -93,7 +93,9 @@ extern "C" int hs_gather_rows(const void *host_alias, int64_t host_blocks, void 
                           reinterpret_cast<uintptr_t>(pool) | (uintptr_t)row_bytes;
   const int64_t warps_needed = count;
   int64_t blocks = ceil_div(warps_needed, kGatherWarps);
-  const int64_t cap = (int64_t)sm_count() * 8;
+  // One small CTA per SM at most: enough host-link reads in flight (4 KiB per
+  // warp) while leaving each SM room for the attention that overlaps the gather.
+  const int64_t cap = (int64_t)sm_count();
   if (blocks > cap) blocks = cap;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if ((align & 15) == 0) gather_kernel<uint4><<<(unsigned)blocks, kGatherThreads, 0, s>>>(p);

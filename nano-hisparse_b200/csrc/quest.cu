@@ -366,7 +366,7 @@ constexpr int kTmaThreads = 512;
 constexpr int kTmaWarps = kTmaThreads / 32;
 constexpr int kTmaStagePages = 16;
 constexpr int kTmaStages = 3;
-constexpr long long kWaitLimit = 1ll << 22;  // bounded mbarrier waits (about a second)
+constexpr long long kWaitLimit = 4000;  // bounded mbarrier waits (each suspends up to ~1 ms)
 
 __device__ __forceinline__ uint32_t smem_addr(const void *p) {
   return (uint32_t)__cvta_generic_to_shared(p);
@@ -379,13 +379,15 @@ __device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, unsigned bytes) {
                "r"(bytes)
                : "memory");
 }
+// try_wait with a suspend-time hint: the warp sleeps until the phase
+// completes (or about 1 ms passes) instead of spinning through instructions.
 __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, unsigned parity) {
   unsigned done;
   asm volatile(
-      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n"
       " selp.u32 %0, 1, 0, p;\n}\n"
       : "=r"(done)
-      : "r"(smem_addr(bar)), "r"(parity)
+      : "r"(smem_addr(bar)), "r"(parity), "r"(1000000u)
       : "memory");
   return done != 0;
 }
@@ -487,29 +489,46 @@ __global__ void __launch_bounds__(kTmaThreads, 1) quest_tma_kernel(QuestParams<T
         }
         float v[32];
 #pragma unroll
-        for (int i = 0; i < kPagesPerItem; ++i) {
-          const int lp = pgi * kPagesPerItem + i;
-          float l[C], h[C];
-          Raw<TKV, C> rl, rh;
-          const bool in = lp < pages;
-          rl.load_shared_full(lo_s + lp * (int)page_elems + kh * D + d0, in);
-          rh.load_shared_full(hi_s + lp * (int)page_elems + kh * D + d0, in);
-          rl.unpack(l);
-          rh.unpack(h);
+        for (int i = 0; i < kPagesPerItem; i += 2) {
+          // pages i and i+1 side by side: one packed fp32x2 FMA serves both
+          float l0[C], h0[C], l1[C], h1[C];
+          {
+            const int lp = pgi * kPagesPerItem + i;
+            Raw<TKV, C> rl0, rh0, rl1, rh1;
+            rl0.load_shared_full(lo_s + lp * (int)page_elems + kh * D + d0, lp < pages);
+            rh0.load_shared_full(hi_s + lp * (int)page_elems + kh * D + d0, lp < pages);
+            rl1.load_shared_full(lo_s + (lp + 1) * (int)page_elems + kh * D + d0, lp + 1 < pages);
+            rh1.load_shared_full(hi_s + (lp + 1) * (int)page_elems + kh * D + d0, lp + 1 < pages);
+            rl0.unpack(l0);
+            rh0.unpack(h0);
+            rl1.unpack(l1);
+            rh1.unpack(h1);
+          }
 #pragma unroll
           for (int hh = 0; hh < kHeadsPerItem; ++hh) {
-            float part = 0.f;
+            if constexpr (kFma) {
+              float2 part = make_float2(0.f, 0.f);
 #pragma unroll
-            for (int c = 0; c < C; ++c) {
-              if constexpr (kFma) {
-                part = __fmaf_rn(qa[hh][c], h[c], c == 0 ? 0.f : part);
-                part = __fmaf_rn(qb[hh][c], l[c], part);
-              } else {
-                const float t = fmaxf(__fmul_rn(qa[hh][c], l[c]), __fmul_rn(qa[hh][c], h[c]));
-                part = c == 0 ? t : __fadd_rn(part, t);
+              for (int c = 0; c < C; ++c) {
+                part = __ffma2_rn(make_float2(qa[hh][c], qa[hh][c]), make_float2(h0[c], h1[c]),
+                                  c == 0 ? make_float2(0.f, 0.f) : part);
+                part = __ffma2_rn(make_float2(qb[hh][c], qb[hh][c]), make_float2(l0[c], l1[c]),
+                                  part);
               }
+              v[i * kHeadsPerItem + hh] = part.x;
+              v[(i + 1) * kHeadsPerItem + hh] = part.y;
+            } else {
+              float p0 = 0.f, p1 = 0.f;
+#pragma unroll
+              for (int c = 0; c < C; ++c) {
+                const float t0 = fmaxf(__fmul_rn(qa[hh][c], l0[c]), __fmul_rn(qa[hh][c], h0[c]));
+                const float t1 = fmaxf(__fmul_rn(qa[hh][c], l1[c]), __fmul_rn(qa[hh][c], h1[c]));
+                p0 = c == 0 ? t0 : __fadd_rn(p0, t0);
+                p1 = c == 0 ? t1 : __fadd_rn(p1, t1);
+              }
+              v[i * kHeadsPerItem + hh] = p0;
+              v[(i + 1) * kHeadsPerItem + hh] = p1;
             }
-            v[i * kHeadsPerItem + hh] = part;
           }
         }
 #pragma unroll
@@ -582,9 +601,8 @@ int launch_tma(QuestParams<TQ, TKV> &p, int C, cudaStream_t stream) {
 #define HS_QUEST_TMA(CC)                                                                  \
   case CC: {                                                                              \
     auto k = quest_tma_kernel<TQ, TKV, CC>;                                               \
-    if (cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != \
-        cudaSuccess)                                                                      \
-      return set_error(HS_ERR_CUDA, "quest: cannot reserve %zu bytes of shared memory", smem); \
+    const int rc = reserve_smem((const void *)k, smem, "quest");                          \
+    if (rc != HS_OK) return rc;                                                           \
     k<<<grid, kTmaThreads, smem, stream>>>(p);                                            \
     break;                                                                                \
   }
@@ -624,10 +642,8 @@ int launch(QuestParams<TQ, TKV> &p, cudaStream_t stream, bool aligned) {
 #define HS_QUEST_CASE(CC)                                                                 \
   case CC: {                                                                              \
     auto k = quest_kernel<TQ, TKV, CC>;                                                   \
-    if (smem > 48 * 1024 &&                                                               \
-        cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != \
-            cudaSuccess)                                                                  \
-      return set_error(HS_ERR_CUDA, "quest: cannot reserve %zu bytes of shared memory", smem); \
+    const int rc = reserve_smem((const void *)k, smem, "quest");                          \
+    if (rc != HS_OK) return rc;                                                           \
     k<<<grid, kThreads, smem, stream>>>(p);                                               \
     break;                                                                                \
   }

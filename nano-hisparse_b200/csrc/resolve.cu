@@ -80,6 +80,7 @@ struct ResolveParams {
   Lengths lengths;
   int page_size;
   int64_t *out_physical, *out_miss_host, *out_miss_device, *out_counts;
+  int64_t *out_ready;  // optional [batch, count]: resident + hot rows, compact
   const int64_t *head_columns;
   int64_t head_count, head_width;
   int64_t *out_head_physical;
@@ -232,8 +233,12 @@ __device__ __forceinline__ void resolve_body(const ResolveParams &p, const Layou
     unsigned long long prefix = block_exclusive_scan<unsigned long long>(local, scan_scratch,
                                                                         &totals);
     int rank = (int)(prefix & kCountMask);
-    for (int j = klo; j < khi; ++j)
-      if (jflags[j] & kMiss) jrank[j] = rank++;
+    int ready = (int)(((prefix >> kCountBits) & kCountMask) + ((prefix >> (2 * kCountBits)) & kCountMask));
+    for (int j = klo; j < khi; ++j) {
+      const uint8_t f = jflags[j];
+      if (f & kMiss) jrank[j] = rank++;
+      else if (f & (kHotHit | kResidentHit)) jrank[j] = ready++;  // rank in the ready list
+    }
   }
   const int misses = (int)(totals & kCountMask);
   // ---- 6. victims: unprotected slots in LRU order, then protected ---------------
@@ -253,13 +258,17 @@ __device__ __forceinline__ void resolve_body(const ResolveParams &p, const Layou
     // only reachable with more positions than hot rows (the cache caps
     // positions at max_union_rows <= hot_rows)
     for (int i = tid; i < K; i += nthreads) out_phys[i] = out_mh[i] = out_md[i] = -1;
+    if (p.out_ready)
+      for (int i = tid; i < K; i += nthreads) p.out_ready[(int64_t)b * K + i] = -1;
     if (tid < 3) out_counts[tid] = 0;
     if (tid == 0) flag(p.status, HS_DEV_MISSES_EXCEED_HOT);
     return;
   }
-  // ---- 7. slots, physical rows, miss plan, tag update -----------------------------
+  // ---- 7. slots, physical rows, miss plan, ready list, tag update --------------------
+  int64_t *out_ready = p.out_ready ? p.out_ready + (int64_t)b * K : nullptr;
   for (int j = tid; j < K; j += nthreads) {
     const uint8_t f = jflags[j];
+    if (out_ready && (f & kResidentHit)) out_ready[jrank[j]] = jphys[j];
     if (!(f & kNeedsHot)) continue;
     int32_t slot;
     if (f & kMiss) {
@@ -275,9 +284,16 @@ __device__ __forceinline__ void resolve_body(const ResolveParams &p, const Layou
       out_mh[r] = jhost[j];
       out_md[r] = hot_phys;
       tags[slot] = (int32_t)jhost[j];
+    } else if (out_ready) {
+      out_ready[jrank[j]] = hot_phys;
     }
   }
   for (int i = misses + tid; i < K; i += nthreads) out_mh[i] = out_md[i] = -1;
+  if (out_ready) {
+    const int ready = (int)(((totals >> kCountBits) & kCountMask) +
+                            ((totals >> (2 * kCountBits)) & kCountMask));
+    for (int i = ready + tid; i < K; i += nthreads) out_ready[i] = -1;
+  }
   if (tid == 0) {
     out_counts[0] = (int64_t)((totals >> (2 * kCountBits)) & kCountMask);
     out_counts[1] = (int64_t)((totals >> kCountBits) & kCountMask);
@@ -405,6 +421,8 @@ __global__ void __launch_bounds__(kResolveThreads) resolve_kernel(ResolveParams 
     // a corrupt LRU permutation cannot be resolved faithfully: tables stay
     // untouched and the plan is empty
     for (int i = tid; i < K; i += nthreads) out_phys[i] = out_mh[i] = out_md[i] = -1;
+    if (p.out_ready)
+      for (int i = tid; i < K; i += nthreads) p.out_ready[(int64_t)b * K + i] = -1;
     if (tid < 3) out_counts[tid] = 0;
     if (tid == 0) flag(p.status, HS_DEV_LRU_CORRUPT);
   } else {
@@ -448,10 +466,8 @@ int resolve_common(ResolveParams &p, size_t workspace_bytes, cudaStream_t stream
       return set_error(HS_ERR_WORKSPACE, "resolve: workspace of %zu bytes < required %zu",
                        workspace_bytes, need);
   }
-  if (smem > 48 * 1024 &&
-      cudaFuncSetAttribute(resolve_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           (int)smem) != cudaSuccess)
-    return set_error(HS_ERR_CUDA, "resolve: cannot reserve %zu bytes of shared memory", smem);
+  const int rc = reserve_smem((const void *)resolve_kernel, smem, "resolve");
+  if (rc != HS_OK) return rc;
   resolve_kernel<<<p.batch, kResolveThreads, smem, stream>>>(p);
   return check_launch("resolve_kernel");
 }
@@ -519,9 +535,9 @@ extern "C" int hs_resolve_rows_batched(int batch, const int32_t *positions, int6
                                        int64_t hot_rows, const int32_t *lengths,
                                        int page_size, int64_t *out_physical,
                                        int64_t *out_miss_host, int64_t *out_miss_device,
-                                       int64_t *out_counts, void *workspace,
-                                       size_t workspace_bytes, int32_t *device_status,
-                                       hs_stream stream) {
+                                       int64_t *out_counts, int64_t *out_ready,
+                                       void *workspace, size_t workspace_bytes,
+                                       int32_t *device_status, hs_stream stream) {
   if (!source_ptrs || !resident_ptrs || !hot_ptrs || !tags_ptrs || !lru_ptrs || !lengths)
     return hs::set_error(HS_ERR_INVALID_ARGUMENT, "resolve: null pointer array or lengths");
   hs::ResolveParams p{};
@@ -543,6 +559,7 @@ extern "C" int hs_resolve_rows_batched(int batch, const int32_t *positions, int6
   p.out_miss_host = out_miss_host;
   p.out_miss_device = out_miss_device;
   p.out_counts = out_counts;
+  p.out_ready = out_ready;
   p.workspace = static_cast<char *>(workspace);
   p.status = device_status;
   return hs::resolve_common(p, workspace_bytes, static_cast<cudaStream_t>(stream));

@@ -45,11 +45,15 @@ _SIGNATURES = {
     "hs_resolve_rows": ([_P, _INT, _I64, _P, _P, _I64, _P, _I64, _P, _P, _I64, _I64, _INT, _P,
                          _P, _P, _P, _P, _I64, _I64, _P, _P, _SZ, _P, _P], _INT),
     "hs_resolve_rows_batched": ([_INT, _P, _I64, _P, _P, _I64, _P, _I64, _P, _P, _I64, _P, _INT,
-                                 _P, _P, _P, _P, _P, _SZ, _P, _P], _INT),
+                                 _P, _P, _P, _P, _P, _P, _SZ, _P, _P], _INT),
     "hs_gather_rows": ([_P, _I64, _P, _I64, _P, _P, _I64, _I64, _INT, _I64, _P, _P], _INT),
     "hs_attend_workspace_bytes": ([_INT, _INT, _INT, _INT, _I64], _SZ),
     "hs_attend_rows": ([_INT, _P, _I64, _INT, _P, _I64, _INT, _P, _I64, _I64, _I64, _P, _I64,
                         _INT, _INT, _INT, _INT, _P, _SZ, _P, _P], _INT),
+    "hs_attend_rows_phase": ([_INT, _P, _I64, _INT, _P, _I64, _INT, _P, _I64, _I64, _P, _INT,
+                              _INT, _INT, _INT, _INT, _INT, _INT, _INT, _P, _SZ, _P, _P], _INT),
+    "hs_attend_merge": ([_INT, _INT, _P, _I64, _INT, _INT, _INT, _INT, _I64, _P, _SZ, _P, _P],
+                        _INT),
 }
 
 _lib = None

@@ -2,10 +2,15 @@
 
 The reference decodes requests one at a time (engine.py:76-126). Here one
 ``DecodeBatch.layer`` call runs the whole per-layer hot path for B requests
-with four batched libhisparse launches — Quest selection, resolver, miss
-gather, attention — and the same ordering protocol as ``RowCache.resolve``:
-the gather runs on the transfer stream after the resolver and after the
-previous readers of the layer's hot rows; attention waits for the gather.
+with batched libhisparse launches — Quest selection, resolver, miss gather,
+attention — ordered like ``RowCache.resolve`` (the gather runs on the
+transfer stream after the resolver and after the previous readers of the
+layer's hot rows) with one refinement: attention is split in two phases. The
+first attends over the rows that need no gather (resident and hot hits, the
+resolver's ready list) on the compute stream while the gather streams the
+misses in; the second attends over the gathered rows after the gather, and a
+merge combines both. The gather only writes hot slots that no selected row
+occupies, so the first phase never reads a row being written.
 Per-request tables stay separate tensors (the per-request API keeps working
 on them); the batch passes them to the kernels as device pointer arrays built
 once. No host synchronisation happens inside ``layer``.
@@ -50,8 +55,16 @@ class DecodeBatch:
     """
 
     def __init__(self, cache: RowCache, request_ids, layers, minimum, maximum, top_pages,
-                 q_heads, keep_sink=True):
+                 q_heads, keep_sink=True, streams=None):
+        """streams: optional (compute, transfer) CUDA streams for this batch; by
+        default the cache's. Batches over disjoint requests with their own
+        streams run concurrently (micro-batch pipelining: one batch's gather
+        overlaps another's selection, resolve and attention)."""
         self.cache, self.request_ids = cache, list(request_ids)
+        if streams is None:
+            self.compute, self.transfer = cache.compute, cache.transfer
+        else:
+            self.compute, self.transfer = streams
         self.device, self.config = cache.device, cache.config
         self.minimum, self.maximum = minimum, maximum
         self.top_pages, self.keep_sink, self.q_heads = top_pages, keep_sink, q_heads
@@ -69,6 +82,7 @@ class DecodeBatch:
         self.physical = torch.empty((b, self.width), dtype=torch.int64, device=dev)
         self.miss_host = torch.empty((b, self.width), dtype=torch.int64, device=dev)
         self.miss_device = torch.empty((b, self.width), dtype=torch.int64, device=dev)
+        self.ready = torch.empty((b, self.width), dtype=torch.int64, device=dev)
         self.quest_ws_bytes = lib.hs_quest_workspace_bytes(b, self.max_pages)
         self.quest_ws = _lib.workspace(self.quest_ws_bytes, dev, zeroed=True)
         self.resolve_ws_bytes = lib.hs_resolve_workspace_bytes(b, self.width, self.hot_rows)
@@ -92,15 +106,16 @@ class DecodeBatch:
         counts: optional int64 [B, 3] CUDA tensor receiving the resolver counts
         (default: the layer's own buffer, see last_counts). timing: optional
         list; when given, (name, start, end) CUDA-event pairs recorded on each
-        launch's own stream are appended for the four stages."""
+        launch's own stream are appended for the stages."""
         cache, cfg, st, lib = self.cache, self.config, self.layers[layer], _lib.load()
-        cache.check_stream()
+        if torch.cuda.current_stream(self.device) != self.compute:
+            raise RuntimeError("DecodeBatch.layer must run on the batch's compute stream")
         b, hq, d = query.shape
         if b != self.batch or hq != self.q_heads or d != cfg.head_dim:
             raise ValueError("query must be [batch, q_heads, head_dim]")
         if out is None:
             out = torch.empty_like(query)
-        compute, transfer = cache.compute, cache.transfer
+        compute, transfer = self.compute, self.transfer
         stream = compute.cuda_stream
         status = self.status.data_ptr()
         if counts is None:
@@ -130,8 +145,8 @@ class DecodeBatch:
             st.table_pages, st.hot_ptrs.data_ptr(), cache.hot_blocks, st.tag_ptrs.data_ptr(),
             st.lru_ptrs.data_ptr(), self.hot_rows, st.lengths.data_ptr(), cfg.page_size,
             self.physical.data_ptr(), self.miss_host.data_ptr(), self.miss_device.data_ptr(),
-            counts.data_ptr(), _lib.ptr(self.resolve_ws), self.resolve_ws_bytes, status,
-            stream))
+            counts.data_ptr(), self.ready.data_ptr(), _lib.ptr(self.resolve_ws),
+            self.resolve_ws_bytes, status, stream))
         t2 = mark(compute)
         resolved = torch.cuda.Event()
         resolved.record(compute)
@@ -147,17 +162,29 @@ class DecodeBatch:
         t4 = mark(transfer)
         st.ready = torch.cuda.Event()
         st.ready.record(transfer)
-        compute.wait_event(st.ready)
+        # phase 0: rows that need no gather, concurrently with the gather
         t5 = mark(compute)
-        _lib.check(lib.hs_attend_rows(
-            b, query.data_ptr(), hq * d, _lib.dtype_code(query.dtype), cache.pool.data_ptr(),
-            cache.pool.shape[0], self._dtype, self.physical.data_ptr(), self.width, 0,
-            self.width, out.data_ptr(), hq * d, hq, cfg.kv_heads, d, cfg.page_size,
-            _lib.ptr(self.attend_ws), self.attend_ws_bytes, status, stream))
+        common = (b, query.data_ptr(), hq * d, _lib.dtype_code(query.dtype), cache.pool.data_ptr(),
+                  cache.pool.shape[0], self._dtype)
+        _lib.check(lib.hs_attend_rows_phase(
+            *common, self.ready.data_ptr(), self.width, self.width, counts.data_ptr(), 3, 0, 2, 0,
+            hq, cfg.kv_heads, d, cfg.page_size, _lib.ptr(self.attend_ws), self.attend_ws_bytes,
+            status, stream))
+        t6 = mark(compute)
+        # phase 1: the gathered rows, then the merge
+        compute.wait_event(st.ready)
+        t7 = mark(compute)
+        _lib.check(lib.hs_attend_rows_phase(
+            *common, self.miss_device.data_ptr(), self.width, self.width, counts.data_ptr(), 3, 2,
+            1, 1, hq, cfg.kv_heads, d, cfg.page_size, _lib.ptr(self.attend_ws),
+            self.attend_ws_bytes, status, stream))
+        _lib.check(lib.hs_attend_merge(
+            b, 2, out.data_ptr(), hq * d, _lib.dtype_code(query.dtype), hq, cfg.kv_heads, d,
+            self.width, _lib.ptr(self.attend_ws), self.attend_ws_bytes, status, stream))
         if timing is not None:
-            t6 = mark(compute)
+            t8 = mark(compute)
             timing += [("quest", t0, t1), ("resolve", t1, t2), ("gather", t3, t4),
-                       ("attend", t5, t6)]
+                       ("attend_ready", t5, t6), ("attend_gathered", t7, t8)]
         st.last_use = torch.cuda.Event()
         st.last_use.record(compute)
         return out
@@ -166,3 +193,65 @@ class DecodeBatch:
         """[layers, B, 3] resolver counts (resident hits, hot hits, misses) of
         the most recent call of each layer."""
         return torch.stack([st.counts for st in self.layers])
+
+
+class DecodeGraph:
+    """One decode step — every layer of every micro-batch — captured once as a
+    CUDA graph and replayed per step, so the host issues one launch per step
+    instead of ~six kernels and a dozen events per (micro-batch, layer).
+
+    batches: DecodeBatch objects over disjoint requests, each with its own
+    streams. Inputs and outputs are static buffers: ``queries[i]`` is
+    [layers, B_i, Hq, D] for batch i, ``outputs[i]`` the same shape, and
+    ``counts[i]`` [layers, B_i, 3] receives the resolver counts of the last
+    replay. Fill ``queries`` (on the replaying stream), call ``replay()``.
+    The step's stream/event ordering is that of DecodeBatch.layer; replays on
+    one stream are serialised, which orders a layer's gather after the
+    previous step's readers of its hot rows.
+    """
+
+    def __init__(self, batches, layers: int, timing: bool = False):
+        self.batches, self.layers = list(batches), layers
+        b0 = self.batches[0]
+        self.device = b0.device
+        dt = b0.config.dtype
+        self.queries = [torch.zeros((layers, bt.batch, bt.q_heads, bt.config.head_dim),
+                                    dtype=dt, device=self.device) for bt in self.batches]
+        self.outputs = [torch.empty_like(q) for q in self.queries]
+        self.counts = [torch.zeros((layers, bt.batch, 3), dtype=torch.int64, device=self.device)
+                       for bt in self.batches]
+        self.timing = [] if timing else None
+        # two eager steps settle lazy state (function attributes, workspaces)
+        # before capture; the events they leave behind are dropped
+        for _ in range(2):
+            self._run(None)
+        torch.cuda.synchronize(self.device)
+        self._reset_events()
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self._run(self.timing)
+        self._reset_events()
+
+    def _reset_events(self):
+        for bt in self.batches:
+            for st in bt.layers:
+                st.ready = st.last_use = None
+
+    def _run(self, timing):
+        caller = torch.cuda.current_stream(self.device)
+        start = torch.cuda.Event()
+        start.record(caller)
+        for bt in self.batches:
+            bt.compute.wait_event(start)
+        for layer in range(self.layers):
+            for i, bt in enumerate(self.batches):
+                with torch.cuda.stream(bt.compute):
+                    bt.layer(layer, self.queries[i][layer], self.outputs[i][layer],
+                             self.counts[i][layer], timing)
+        for bt in self.batches:
+            done = torch.cuda.Event()
+            done.record(bt.compute)
+            caller.wait_event(done)
+
+    def replay(self):
+        self.graph.replay()

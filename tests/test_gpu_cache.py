@@ -163,3 +163,62 @@ def test_decode_batch_against_oracle_full_step():
             assert cache.tables[r, 0].lru.tolist() == lrus[r].tolist()
         assert batch.last_counts()[0].tolist() == counts.tolist()
     assert torch.equal(cache.pool.cpu(), pool_cpu)
+
+
+def test_decode_graph_replay_matches_eager_steps():
+    """A whole step captured as a CUDA graph (two micro-batches on their own
+    streams) gives the same outputs, counts and tables as eager DecodeBatch
+    calls on an identical cache."""
+    from hisparse_b200.batched import DecodeGraph
+
+    b, layers, length, p, hkv, d, hq, top = 4, 2, 3000, 16, 8, 128, 32, 16
+    config, hot, host, placement, meta = _build(5, b, layers, length, p, hkv, d, 512, 0.25,
+                                                torch.bfloat16)
+    caches = [_cache(config, hot, host, placement, length) for _ in range(2)]
+    mins = {r: meta[r][0].to(DEV) for r in range(b)}
+    maxs = {r: meta[r][1].to(DEV) for r in range(b)}
+    groups = [[0, 2], [1, 3]]
+
+    def batches(cache):
+        out = []
+        for g in groups:
+            streams = (torch.cuda.Stream(), torch.cuda.Stream())
+            with torch.cuda.stream(streams[0]):
+                out.append(DecodeBatch(cache, g, layers, {r: mins[r] for r in g},
+                                       {r: maxs[r] for r in g}, top, hq, streams=streams))
+        return out
+
+    eager, captured = batches(caches[0]), batches(caches[1])
+    graph = DecodeGraph(captured, layers)  # runs two eager warm-up steps on caches[1]
+    gen = torch.Generator().manual_seed(11)
+    warm = [torch.randn(layers, b, hq, d, generator=gen).to(torch.bfloat16) for _ in range(2)]
+    steps = [torch.randn(layers, b, hq, d, generator=gen).to(torch.bfloat16) for _ in range(3)]
+    torch.cuda.synchronize()
+
+    def eager_step(q):
+        outs = []
+        for layer in range(layers):
+            for i, bt in enumerate(eager):
+                with torch.cuda.stream(bt.compute):
+                    outs.append((i, layer, bt.layer(layer, q[layer][groups[i]].to(DEV).contiguous())))
+        torch.cuda.synchronize()
+        return outs
+
+    # the graph's warm-up used zero queries: replay them on the eager side too
+    zeros = torch.zeros(layers, b, hq, d, dtype=torch.bfloat16)
+    for _ in range(2):
+        eager_step(zeros)
+    for q in steps:
+        ref = eager_step(q)
+        for i, g in enumerate(groups):
+            graph.queries[i].copy_(q[:, g].to(DEV))
+        graph.replay()
+        torch.cuda.synchronize()
+        for i, layer, out in ref:
+            assert torch.equal(graph.outputs[i][layer], out)
+    for key in caches[0].tables:
+        assert torch.equal(caches[0].tables[key].tags, caches[1].tables[key].tags)
+        assert torch.equal(caches[0].tables[key].lru, caches[1].tables[key].lru)
+    assert torch.equal(caches[0].pool, caches[1].pool)
+    del warm
+    assert not _lib.device_flags(DEV)
