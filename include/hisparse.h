@@ -253,6 +253,25 @@ HS_API int hs_attend_merge(int batch, int phases, void *out, int64_t out_batch_s
                            int64_t count, void *workspace, size_t workspace_bytes,
                            int32_t *device_status, hs_stream stream);
 
+/* hs_attend_rows without a caller workspace: no counterpart in the reference
+ * (whose Triton attention needs no scratch). For callers with no device
+ * allocator at hand — a bare FFI binding of this library, or a process whose
+ * device memory is all committed to its pools — the split partials live in a
+ * fixed 16 MiB array in the library's device memory, one per device, and the
+ * call allocates nothing. A call needing more scratch than that
+ * (hs_attend_workspace_bytes > 16 MiB) returns HS_ERR_WORKSPACE. The first
+ * call on a device looks up the array's address (make it before capturing a
+ * stream). All calls on a device share the array: calls that can overlap on
+ * the GPU race and must be ordered by the caller. Nothing in the array needs
+ * to start at zero. Arguments and results are those of hs_attend_rows. */
+HS_API int hs_attend_rows_static(int batch, const void *query, int64_t query_batch_stride,
+                                 int query_dtype, const void *pool, int64_t pool_blocks,
+                                 int kv_dtype, const int64_t *rows, int64_t rows_batch_stride,
+                                 int64_t rows_head_stride, int64_t count, void *out,
+                                 int64_t out_batch_stride, int q_heads, int kv_heads,
+                                 int head_dim, int page_size, int32_t *device_status,
+                                 hs_stream stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -9,6 +9,7 @@
 // Softmax and accumulation are fp32.
 #include <math.h>
 
+#include <mutex>
 #include <type_traits>
 
 #include "common.cuh"
@@ -749,4 +750,81 @@ extern "C" int hs_attend_merge(int batch, int phases, void *out, int64_t out_bat
   p.out = out;
   p.out_batch_stride = out_batch_stride;
   return run_merge(p, query_dtype, static_cast<cudaStream_t>(stream));
+}
+
+// ---- hs_attend_rows_static: the same attention with library-owned scratch ----
+// Some callers cannot hand this library a workspace. A host that binds only the
+// C ABI through a bare FFI stub (ctypes, cgo, JNI) has no device allocator of
+// its own, and a serving process that has handed all of the device's memory to
+// its KV pool cannot grow that memory for a per-call buffer. For them the
+// split partials live in a fixed array in the library's own device memory: this
+// entry point calls no allocator. The array exists once per device; calls on one
+// device share it, so calls that may overlap on the GPU (different streams)
+// race on it and must be ordered by the caller. Nothing in it needs to start at
+// zero: every launch writes the partials and split counts before the merge
+// reads them.
+namespace hs {
+namespace {
+
+constexpr size_t kStaticScratchBytes = size_t(16) << 20;  // per device
+constexpr int kScratchDevices = 64;
+static __device__ __align__(256) unsigned char g_attend_scratch[kStaticScratchBytes];
+
+std::mutex g_scratch_lock;
+void *g_scratch_address[kScratchDevices];
+
+// Device address of this device's scratch array, looked up once per device (the
+// first call on a device does this set-up; a caller that captures streams makes
+// that first call before capturing).
+int static_scratch(void **address) {
+  int dev = -1;
+  cudaError_t err = cudaGetDevice(&dev);
+  if (err != cudaSuccess) {
+    cudaGetLastError();
+    return set_error(HS_ERR_CUDA, "attend (static scratch): no current device: %s",
+                     cudaGetErrorString(err));
+  }
+  if (dev < 0 || dev >= kScratchDevices)
+    return set_error(HS_ERR_UNSUPPORTED, "attend (static scratch): device %d >= %d", dev,
+                     kScratchDevices);
+  std::lock_guard<std::mutex> guard(g_scratch_lock);
+  if (g_scratch_address[dev] == nullptr) {
+    void *p = nullptr;
+    err = cudaGetSymbolAddress(&p, g_attend_scratch);
+    if (err != cudaSuccess || p == nullptr) {
+      cudaGetLastError();
+      return set_error(HS_ERR_CUDA,
+                       "attend (static scratch): cannot resolve the scratch array on device "
+                       "%d: %s", dev, cudaGetErrorString(err));
+    }
+    g_scratch_address[dev] = p;
+  }
+  *address = g_scratch_address[dev];
+  return HS_OK;
+}
+
+}  // namespace
+}  // namespace hs
+
+extern "C" int hs_attend_rows_static(int batch, const void *query, int64_t query_batch_stride,
+                                     int query_dtype, const void *pool, int64_t pool_blocks,
+                                     int kv_dtype, const int64_t *rows,
+                                     int64_t rows_batch_stride, int64_t rows_head_stride,
+                                     int64_t count, void *out, int64_t out_batch_stride,
+                                     int q_heads, int kv_heads, int head_dim, int page_size,
+                                     int32_t *device_status, hs_stream stream) {
+  using namespace hs;
+  const size_t need = hs_attend_workspace_bytes(batch, q_heads, kv_heads, head_dim, count);
+  if (need > kStaticScratchBytes)
+    return set_error(HS_ERR_WORKSPACE,
+                     "attend (static scratch): this call needs %zu bytes of scratch, more "
+                     "than the library's fixed %zu; use hs_attend_rows with a workspace",
+                     need, kStaticScratchBytes);
+  void *scratch = nullptr;
+  const int rc = static_scratch(&scratch);
+  if (rc != HS_OK) return rc;
+  return hs_attend_rows(batch, query, query_batch_stride, query_dtype, pool, pool_blocks,
+                        kv_dtype, rows, rows_batch_stride, rows_head_stride, count, out,
+                        out_batch_stride, q_heads, kv_heads, head_dim, page_size, scratch,
+                        kStaticScratchBytes, device_status, stream);
 }
