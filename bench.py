@@ -41,6 +41,7 @@ HOT_ROWS = 2 * 2048               # reference default: 2 x max_union_rows
 RESIDENT_FRACTION = 0.25
 DTYPE = torch.bfloat16
 MICRO = 2  # request groups pipelined on separate streams
+HOST_STORE = {}  # size of the pinned host store actually allocated (set by build_workload)
 
 
 def workload_config():
@@ -58,6 +59,7 @@ def workload_config():
         "l2": "inputs larger than L2 (about 12 GiB of metadata and KV rows read per step)",
         "parallelism": "requests sharded over ranks, no collective on the hot path",
         "microbatches": MICRO,
+        **({"host_store": HOST_STORE} if HOST_STORE else {}),
     }
 
 
@@ -119,6 +121,52 @@ class ClockSampler:
 # ---------------------------------------------------------------------------
 # GPU arm
 # ---------------------------------------------------------------------------
+def available_host_bytes():
+    """Host RAM this process may still use: MemAvailable, capped by the
+    cgroup's limit when the container has one."""
+    avail = None
+    try:
+        for line in Path("/proc/meminfo").read_text().splitlines():
+            if line.startswith("MemAvailable:"):
+                avail = int(line.split()[1]) * 1024
+    except OSError:
+        pass
+    for limit_file, usage_file in (("/sys/fs/cgroup/memory.max", "/sys/fs/cgroup/memory.current"),
+                                   ("/sys/fs/cgroup/memory/memory.limit_in_bytes",
+                                    "/sys/fs/cgroup/memory/memory.usage_in_bytes")):
+        try:
+            limit = Path(limit_file).read_text().strip()
+            usage = int(Path(usage_file).read_text().strip())
+        except (OSError, ValueError):
+            continue
+        if limit.isdigit() and int(limit) < (1 << 60):
+            room = int(limit) - usage
+            avail = room if avail is None else min(avail, room)
+        break
+    return avail
+
+
+def host_store_pages(wanted_pages, page_bytes, log):
+    """Distinct pinned host pages this rank allocates. The full store is
+    REQUESTS x LAYERS x CONTEXT rows (64 GiB per rank for configuration 2);
+    when all ranks of the node would not fit in half of the free host RAM, the
+    (request, layer) units share a smaller store (unit pages wrap around it).
+    The rows moved per step, and so the host-link bytes, are unchanged."""
+    local_world = int(os.environ.get("LOCAL_WORLD_SIZE", os.environ.get("WORLD_SIZE", 1)))
+    avail = available_host_bytes()
+    if avail is None:
+        return wanted_pages
+    budget = avail // 2 // max(local_world, 1)
+    pages = min(wanted_pages, budget // page_bytes)
+    if pages < wanted_pages:
+        log(f"host RAM: {avail / 2**30:.0f} GiB free for {local_world} rank(s); host store "
+            f"shared by the units ({pages * page_bytes / 2**30:.1f} GiB per rank)")
+    if pages < 4 * math.ceil(CONTEXT / PAGE):
+        raise RuntimeError(f"not enough host RAM for the pinned host store "
+                           f"({avail / 2**30:.1f} GiB free, {local_world} rank(s))")
+    return pages
+
+
 def build_workload(device, seed, log):
     from hisparse_b200 import CacheConfig, DecodeBatch, HotConfig, RowCache
 
@@ -127,7 +175,11 @@ def build_workload(device, seed, log):
     hot_blocks = hot.hot_blocks(PAGE)
     resident_pages = int(round(n * RESIDENT_FRACTION))
     units = REQUESTS * LAYERS
-    config = CacheConfig(gpu_pages=units * (resident_pages + hot_blocks), host_pages=units * n,
+    page_bytes = 2 * PAGE * KV_HEADS * HEAD_DIM * 2
+    host_pages = host_store_pages(units * n, page_bytes, log)
+    HOST_STORE.update(gib_per_rank=round(host_pages * page_bytes / 2**30, 2),
+                      shared_by_units=host_pages < units * n)
+    config = CacheConfig(gpu_pages=units * (resident_pages + hot_blocks), host_pages=host_pages,
                          page_size=PAGE, kv_heads=KV_HEADS, head_dim=HEAD_DIM,
                          device=str(device), dtype=DTYPE,
                          index_budget_bytes=1 << 40)
@@ -145,7 +197,7 @@ def build_workload(device, seed, log):
     t0 = time.time()
     for r in range(REQUESTS):
         for layer in range(LAYERS):
-            base = (r * LAYERS + layer) * n
+            base = ((r * LAYERS + layer) * n) % (host_pages - n + 1)
             kv = torch.randn((n, 2, PAGE, KV_HEADS, HEAD_DIM), generator=gen, device=device,
                              dtype=torch.float32).to(DTYPE)
             mins[r][layer] = kv[:, 0].amin(1)
@@ -214,8 +266,13 @@ def run_gpu(args, rank, world, local_rank, log):
 
     from hisparse_b200 import _lib
 
+    from hisparse_b200.sharding import bind_to_device_node
+
     device = torch.device("cuda", local_rank)
     torch.cuda.set_device(device)
+    # pinned host store on the GPU's own NUMA node (first touch by these CPUs)
+    local_cpus = bind_to_device_node(local_rank)
+    HOST_STORE["numa_local_cpus"] = len(local_cpus) if local_cpus else None
     hbm_peak, hbm_source = measured_peaks()
     link_peak = hostlink_peak(device)
     cache, mins, maxs = build_workload(device, 1 + rank, log)
@@ -533,7 +590,9 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
                                 device_id=torch.device("cuda", local_rank))
     try:
+        all_cpus = os.sched_getaffinity(0)
         result = run_gpu(args, rank, world, local_rank, log)
+        os.sched_setaffinity(0, all_cpus)  # the CPU baseline uses every host core
         if rank == 0:
             if world == 1 and not args.no_cpu_baseline:
                 result["cpu_baseline"] = cpu_sample(log=log)

@@ -5,17 +5,18 @@
 // Reference: nano_hisparse/row_kernels.py:35-70 (_gather, gather_rows) and the
 // CPU loop of hybrid.py:452-459. The reference runs min(n, 64) programs and
 // recompiles per plan width; here the plan width is a runtime argument and
-// the grid has one 4-warp CTA per SM. One warp moves one row: all 2*row_bytes
-// of it are loaded (16-byte vectors when the layout allows) before any store,
-// so each warp keeps up to 4 KiB of host-link reads in flight.
+// the grid has one 2-warp CTA per SM. One warp moves one row, K and V planes
+// side by side: up to 4 KiB of host-link reads in flight per warp (16-byte
+// vectors when the layout allows), about 1 MiB over the grid — several times
+// the link's bandwidth-latency product.
 #include "common.cuh"
 
 namespace hs {
 namespace {
 
-constexpr int kGatherThreads = 128;
+constexpr int kGatherThreads = 64;
 constexpr int kGatherWarps = kGatherThreads / 32;
-constexpr int kUnroll = 8;  // vectors per lane in flight
+constexpr int kUnroll = 4;  // vectors per lane and plane in flight
 
 struct GatherParams {
   const char *host;
@@ -29,12 +30,15 @@ struct GatherParams {
   int32_t *status;
 };
 
+// Two warps of at most 64 registers (4 K registers a CTA): the gather CTAs of
+// two micro-batches fit on an SM beside a Quest or attention CTA, so the
+// kernels that overlap the gather are not held back waiting for its registers.
 template <typename V>
-__global__ void __launch_bounds__(kGatherThreads) gather_kernel(GatherParams p) {
+__global__ void __launch_bounds__(kGatherThreads, 16) gather_kernel(GatherParams p) {
   const int lane = threadIdx.x & 31;
   const int64_t warp = (int64_t)blockIdx.x * kGatherWarps + (threadIdx.x >> 5);
   const int64_t warps = (int64_t)gridDim.x * kGatherWarps;
-  const int64_t vecs = p.row_bytes / (int64_t)sizeof(V);  // per plane
+  const int vecs = (int)(p.row_bytes / (int64_t)sizeof(V));  // per plane
   const int64_t plane_stride = (int64_t)p.page_size * p.row_bytes;
   for (int64_t e = warp; e < p.count; e += warps) {
     const int64_t h = p.miss_host[e], d = p.miss_device[e];
@@ -46,25 +50,26 @@ __global__ void __launch_bounds__(kGatherThreads) gather_kernel(GatherParams p) 
     }
     const char *src = p.host + (hb * 2 * p.page_size + h % p.page_size) * p.row_bytes;
     char *dst = p.pool + (db * 2 * p.page_size + d % p.page_size) * p.row_bytes;
-    const int64_t total = 2 * vecs;  // K plane then V plane
-    for (int64_t c0 = 0; c0 < total; c0 += 32 * kUnroll) {
-      V buf[kUnroll];
+    const V *k_src = reinterpret_cast<const V *>(src);
+    const V *v_src = reinterpret_cast<const V *>(src + plane_stride);
+    V *k_dst = reinterpret_cast<V *>(dst);
+    V *v_dst = reinterpret_cast<V *>(dst + plane_stride);
+    for (int c0 = lane; c0 < vecs; c0 += 32 * kUnroll) {
+      V k[kUnroll], v[kUnroll];
 #pragma unroll
       for (int u = 0; u < kUnroll; ++u) {
-        const int64_t c = c0 + u * 32 + lane;
-        if (c < total) {
-          const int64_t plane = c >= vecs;
-          buf[u] = *reinterpret_cast<const V *>(src + plane * plane_stride +
-                                                (c - plane * vecs) * (int64_t)sizeof(V));
+        const int c = c0 + 32 * u;
+        if (c < vecs) {
+          k[u] = __ldcs(k_src + c);  // host rows are read once: stream past the caches
+          v[u] = __ldcs(v_src + c);
         }
       }
 #pragma unroll
       for (int u = 0; u < kUnroll; ++u) {
-        const int64_t c = c0 + u * 32 + lane;
-        if (c < total) {
-          const int64_t plane = c >= vecs;
-          *reinterpret_cast<V *>(dst + plane * plane_stride +
-                                 (c - plane * vecs) * (int64_t)sizeof(V)) = buf[u];
+        const int c = c0 + 32 * u;
+        if (c < vecs) {
+          k_dst[c] = k[u];
+          v_dst[c] = v[u];
         }
       }
     }
@@ -93,8 +98,8 @@ extern "C" int hs_gather_rows(const void *host_alias, int64_t host_blocks, void 
                           reinterpret_cast<uintptr_t>(pool) | (uintptr_t)row_bytes;
   const int64_t warps_needed = count;
   int64_t blocks = ceil_div(warps_needed, kGatherWarps);
-  // One small CTA per SM at most: enough host-link reads in flight (4 KiB per
-  // warp) while leaving each SM room for the attention that overlaps the gather.
+  // One small CTA per SM at most: enough host-link reads in flight while leaving
+  // each SM room for the kernels that overlap the gather.
   const int64_t cap = (int64_t)sm_count();
   if (blocks > cap) blocks = cap;
   cudaStream_t s = static_cast<cudaStream_t>(stream);

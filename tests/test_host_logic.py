@@ -106,3 +106,16 @@ def test_sharding_helpers():
     assert min(lengths) >= 4096 and max(lengths) <= 131072
     assert 8000 < sorted(lengths)[128] < 32000
     assert lengths == lognormal_lengths(256, 16384, 4096, 131072, seed=4)
+
+
+def test_numa_topology_parsing(tmp_path):
+    from hisparse_b200.sharding import parse_cpulist, pci_local_cpus
+
+    assert parse_cpulist("0-3,8,10-11\n") == {0, 1, 2, 3, 8, 10, 11}
+    assert parse_cpulist("") == set()
+    node = tmp_path / "0000:53:00.0"
+    node.mkdir()
+    (node / "local_cpulist").write_text("56-111,168-223\n")
+    cpus = pci_local_cpus(0, 0x53, 0, tmp_path)
+    assert len(cpus) == 112 and 56 in cpus and 223 in cpus and 0 not in cpus
+    assert pci_local_cpus(0, 0x54, 0, tmp_path) is None
