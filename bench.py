@@ -41,6 +41,7 @@ HOT_ROWS = 2 * 2048               # reference default: 2 x max_union_rows
 RESIDENT_FRACTION = 0.25
 DTYPE = torch.bfloat16
 MICRO = 2  # request groups pipelined on separate streams
+TRANSFER = "shared"  # the micro-batches' gathers share one transfer stream
 HOST_STORE = {}  # size of the pinned host store actually allocated (set by build_workload)
 
 
@@ -58,7 +59,7 @@ def workload_config():
         "kv": "N(0,1) bf16, page min/max metadata from K (seed 1)",
         "l2": "inputs larger than L2 (about 12 GiB of metadata and KV rows read per step)",
         "parallelism": "requests sharded over ranks, no collective on the hot path",
-        "microbatches": MICRO,
+        "microbatches": MICRO, "transfer_streams": TRANSFER,
         **({"host_store": HOST_STORE} if HOST_STORE else {}),
     }
 
@@ -226,8 +227,10 @@ def make_batches(cache, mins, maxs, micro, device):
 
     groups = [list(range(REQUESTS))[i::micro] for i in range(micro)]
     batches = []
+    shared = torch.cuda.Stream(device=device)
     for g in groups:
-        streams = (torch.cuda.Stream(device=device), torch.cuda.Stream(device=device))
+        transfer = shared if TRANSFER == "shared" else torch.cuda.Stream(device=device)
+        streams = (torch.cuda.Stream(device=device), transfer)
         with torch.cuda.stream(streams[0]):
             batches.append(DecodeBatch(cache, g, LAYERS, {r: mins[r] for r in g},
                                        {r: maxs[r] for r in g}, TOP_PAGES, Q_HEADS,
@@ -545,7 +548,7 @@ def cpu_sample(seed=1, budget_s=10.0, threads=None, log=print):
 
 
 def main():
-    global REQUESTS, LAYERS, MICRO
+    global REQUESTS, LAYERS, MICRO, TRANSFER
     parser = argparse.ArgumentParser(description=__doc__.split("\n\n")[0])
     parser.add_argument("--gpus", type=int, default=1)
     parser.add_argument("--steps", type=int, default=10)
@@ -556,10 +559,14 @@ def main():
                         help="independent request groups pipelined on separate streams")
     # Smaller request/layer counts are for ncu captures only; the bench line of
     # configuration 2 uses the defaults.
+    parser.add_argument("--transfer", choices=["shared", "separate"], default=TRANSFER,
+                        help="one transfer stream for all micro-batches (gathers take the "
+                             "host link in turn) or one each")
     parser.add_argument("--requests", type=int, default=REQUESTS)
     parser.add_argument("--layers", type=int, default=LAYERS)
     args = parser.parse_args()
     REQUESTS, LAYERS, MICRO = args.requests, args.layers, args.microbatches
+    TRANSFER = args.transfer
     rank = int(os.environ.get("RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", 1))
     local_rank = int(os.environ.get("LOCAL_RANK", 0))

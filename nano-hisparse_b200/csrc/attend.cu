@@ -195,7 +195,6 @@ __global__ void __launch_bounds__(kAttendThreads) attend_split_kernel(AttendPara
     for (int c = 0; c < C; ++c) red_acc[warp][g][d0 + c] = acc[g][c];
   }
   __syncthreads();
-  const int stride = D + 2;
   for (int idx = threadIdx.x; idx < hn * (D + 2); idx += blockDim.x) {
     const int g = idx / (D + 2), e = idx % (D + 2);
     float mm = -INFINITY;
@@ -473,7 +472,6 @@ __global__ void __launch_bounds__(kMmaThreads, 1) attend_mma_kernel(AttendParams
   if (!active) return;
 
   // ---- one (max, sum, O) partial per head of this warp ----
-  const int stride = 128 + 2;
 #pragma unroll
   for (int hh = 0; hh < 2; ++hh) {
     float l = l_run[hh];
@@ -495,35 +493,63 @@ __global__ void __launch_bounds__(kMmaThreads, 1) attend_mma_kernel(AttendParams
   }
 }
 
+// Merge: one 128-thread CTA per (request, query head). Thread t reads the
+// (max, sum) of partial t (phase 0's splits, then phase 1's; at most
+// 2 * kMaxSplits = 128 partials), the block reduces the global max and the
+// denominator, and each thread then sums its output elements over the weighted
+// partials — three dependent steps instead of a serial walk over the splits.
+constexpr int kMergeThreads = 2 * kMaxSplits;
+
 template <typename TQ>
-__global__ void attend_merge_kernel(AttendParams p) {
-  const int h = blockIdx.x, b = blockIdx.y;
-  const int D = p.head_dim, stride = D + 2;
-  float mm = -INFINITY;
-  for (int ph = 0; ph < p.phases; ++ph) {
-    p.phase = ph;
-    const int splits = p.phase_splits[ph];
-    for (int s = 0; s < splits; ++s) mm = fmaxf(mm, partial_slot(p, b, h, s)[D]);
+__global__ void __launch_bounds__(kMergeThreads) attend_merge_kernel(AttendParams p) {
+  __shared__ float weight[kMergeThreads];
+  __shared__ float reduce[kMergeThreads / 32];
+  __shared__ float result[2];
+  const int h = blockIdx.x, b = blockIdx.y, t = threadIdx.x;
+  const int lane = t & 31, warp = t >> 5;
+  const int D = p.head_dim;
+  const int s0 = p.phase_splits[0], s1 = p.phases > 1 ? p.phase_splits[1] : 0;
+  const int total = s0 + s1;
+  auto partial = [&](int i) {
+    p.phase = i < s0 ? 0 : 1;
+    return partial_slot(p, b, h, i < s0 ? i : i - s0);
+  };
+  float m = -INFINITY, l = 0.f;
+  if (t < total) {
+    const float *part = partial(t);
+    m = part[D];
+    l = part[D + 1];
   }
-  float denom = 0.f;
-  for (int ph = 0; ph < p.phases; ++ph) {
-    p.phase = ph;
-    const int splits = p.phase_splits[ph];
-    for (int s = 0; s < splits; ++s) {
-      const float *part = partial_slot(p, b, h, s);
-      if (part[D] != -INFINITY) denom += expf(part[D] - mm) * part[D + 1];
-    }
+  float mm = warp_max(m);
+  if (lane == 0) reduce[warp] = mm;
+  __syncthreads();
+  if (t == 0) {
+    float v = reduce[0];
+    for (int w = 1; w < kMergeThreads / 32; ++w) v = fmaxf(v, reduce[w]);
+    result[0] = v;
   }
+  __syncthreads();
+  mm = result[0];
+  const float w = m == -INFINITY ? 0.f : expf(m - mm);
+  weight[t] = w;
+  const float dl = warp_xor_tree_sum(w * l);
+  __syncthreads();  // reduce[] is reused below
+  if (lane == 0) reduce[warp] = dl;
+  __syncthreads();
+  if (t == 0) {
+    float v = 0.f;
+    for (int i = 0; i < kMergeThreads / 32; ++i) v += reduce[i];
+    result[1] = v;
+  }
+  __syncthreads();
+  const float denom = result[1];
   TQ *out = static_cast<TQ *>(p.out) + (int64_t)b * p.out_batch_stride + (int64_t)h * D;
-  for (int d = threadIdx.x; d < D; d += blockDim.x) {
+  for (int d = t; d < D; d += kMergeThreads) {
     float num = 0.f;
-    for (int ph = 0; ph < p.phases; ++ph) {
-      p.phase = ph;
-      const int splits = p.phase_splits[ph];
-      for (int s = 0; s < splits; ++s) {
-        const float *part = partial_slot(p, b, h, s);
-        if (part[D] != -INFINITY) num += expf(part[D] - mm) * part[d];
-      }
+#pragma unroll 4
+    for (int i = 0; i < total; ++i) {
+      const float wi = weight[i];
+      if (wi != 0.f) num += wi * partial(i)[d];
     }
     out[d] = from_f32<TQ>(denom > 0.f ? num / denom : 0.f);
   }
@@ -578,7 +604,7 @@ int launch(AttendParams &p, cudaStream_t stream) {
 }
 
 template <typename TQ> int launch_merge(AttendParams &p, cudaStream_t stream) {
-  attend_merge_kernel<TQ><<<dim3(p.q_heads, p.batch), 128, 0, stream>>>(p);
+  attend_merge_kernel<TQ><<<dim3(p.q_heads, p.batch), kMergeThreads, 0, stream>>>(p);
   return check_launch("attend_merge_kernel");
 }
 

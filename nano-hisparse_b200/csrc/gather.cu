@@ -100,7 +100,11 @@ extern "C" int hs_gather_rows(const void *host_alias, int64_t host_blocks, void 
   int64_t blocks = ceil_div(warps_needed, kGatherWarps);
   // One small CTA per SM at most: enough host-link reads in flight while leaving
   // each SM room for the kernels that overlap the gather.
+#ifdef HS_GATHER_MAX_CTAS
+  const int64_t cap = HS_GATHER_MAX_CTAS;
+#else
   const int64_t cap = (int64_t)sm_count();
+#endif
   if (blocks > cap) blocks = cap;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if ((align & 15) == 0) gather_kernel<uint4><<<(unsigned)blocks, kGatherThreads, 0, s>>>(p);
