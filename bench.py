@@ -42,6 +42,13 @@ RESIDENT_FRACTION = 0.25
 DTYPE = torch.bfloat16
 MICRO = 2  # request groups pipelined on separate streams
 TRANSFER = "shared"  # the micro-batches' gathers share one transfer stream
+SETTLE_STEPS = 12  # untimed steps that fill the hot buffers before the warm-up steps
+# PCIe read bytes per byte the gather stores into the pool: ncu's
+# pcie__read_bytes.sum / l1tex__t_bytes_pipe_lsu_mem_global_op_st.sum on four
+# gather launches of configuration 2 at one layer, 1.09375 on each
+# (profiles/gather_kernel_config2_one_layer.md); the roofline traffic of a
+# launch is this ratio times its bytes
+PCIE_READ_PER_GATHERED_BYTE = 1.09375
 HOST_STORE = {}  # size of the pinned host store actually allocated (set by build_workload)
 
 
@@ -60,6 +67,7 @@ def workload_config():
         "l2": "inputs larger than L2 (about 12 GiB of metadata and KV rows read per step)",
         "parallelism": "requests sharded over ranks, no collective on the hot path",
         "microbatches": MICRO, "transfer_streams": TRANSFER,
+        "settle_steps": SETTLE_STEPS,
         **({"host_store": HOST_STORE} if HOST_STORE else {}),
     }
 
@@ -283,8 +291,13 @@ def run_gpu(args, rank, world, local_rank, log):
     steps, warmup = args.steps, args.warmup
     gen = torch.Generator(device=device).manual_seed(1000 + rank)
     total = steps + warmup
-    queries = torch.randn((total, LAYERS, REQUESTS, Q_HEADS, HEAD_DIM), generator=gen,
-                          device=device, dtype=torch.float32).to(DTYPE)
+    # fresh queries for every pass (timed graph steps, the eager per-stage pass,
+    # the instrumented gather pass, the end-to-end steps): a repeated query would
+    # find its rows already hot and gather less than a real step
+    eager_base, roof_base, e2e_base = total, total + steps, 2 * total + steps
+    settle_base = 3 * total + steps
+    queries = torch.randn((3 * total + steps + SETTLE_STEPS, LAYERS, REQUESTS, Q_HEADS,
+                           HEAD_DIM), generator=gen, device=device, dtype=torch.float32).to(DTYPE)
     counts = torch.zeros((total, LAYERS, REQUESTS, 3), dtype=torch.int64, device=device)
     compute = cache.compute
 
@@ -302,18 +315,22 @@ def run_gpu(args, rank, world, local_rank, log):
 
     from hisparse_b200.batched import DecodeGraph
 
-    gq = [queries[:, :, g].contiguous() for g in groups]          # [total, L, Bg, Hq, D]
+    gq = [queries[:, :, g].contiguous() for g in groups]          # [sets, L, Bg, Hq, D]
     graph = DecodeGraph(batches, LAYERS)
     log("captured one decode step as a CUDA graph")
 
-    def run_steps(first, last):
+    def run_steps(first, last, g_=graph, base=0, out=counts):
         for s in range(first, last):
             for i in range(len(groups)):
-                graph.queries[i].copy_(gq[i][s % total])
-            graph.replay()
+                g_.queries[i].copy_(gq[i][base + s])
+            g_.replay()
             for i, g in enumerate(groups):
-                counts[s % total, :, g] = graph.counts[i]
+                out[s, :, g] = g_.counts[i]
 
+    # decode steady state: the hot buffers fill up (4096 rows a unit, ~440 misses
+    # a step) before the W warm-up steps, as they are after the first dozen tokens
+    settle = torch.zeros((SETTLE_STEPS, LAYERS, REQUESTS, 3), dtype=torch.int64, device=device)
+    run_steps(0, SETTLE_STEPS, graph, settle_base, settle)
     run_steps(0, warmup)
     barrier()
     # ---- timed region: K steps, device-resident inputs ------------------------------
@@ -328,24 +345,59 @@ def run_gpu(args, rank, world, local_rank, log):
     clocks = sampler.stop()
     elapsed_ms = max_over_ranks(start.elapsed_time(end))
     timed_counts = counts[warmup:].cpu().numpy()  # [steps, L, B, 3]
+    row_bytes = 2 * KV_HEADS * HEAD_DIM * 2
 
-    # ---- per-stage device time: the same steps run eagerly with CUDA events on
-    # each launch's stream; a spin kernel ahead of every layer keeps the streams
-    # busy while the host enqueues, so no host gap lands inside a measured span
+    # ---- gather roofline: the same step captured with CUDA events around every
+    # gather launch (on the transfer stream it runs on), replayed W + K times on
+    # fresh queries; the events hold the last step's 64 launch durations. (The
+    # event nodes cost about 3% of a step, so the headline region above runs the
+    # uninstrumented graph.)
+    graph_t = DecodeGraph(batches, LAYERS, timing=("gather",))
+    roof_counts = torch.zeros_like(counts)
+    run_steps(0, warmup, graph_t, roof_base, roof_counts)
+    barrier()
+    r0, r1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    r0.record(compute)
+    run_steps(warmup, total, graph_t, roof_base, roof_counts)
+    r1.record(compute)
+    barrier()
+    roof_step_ms = r0.elapsed_time(r1) / steps
+    last = roof_counts[total - 1].cpu().numpy()
+    nb = len(groups)
+    live = []
+    for idx, (_, a, b) in enumerate(graph_t.timing):
+        layer, i = divmod(idx, nb)
+        live.append((int(last[layer, groups[i], 2].sum()) * row_bytes, a, b))
+    live_ms = [a.elapsed_time(b) for _, a, b in live]
+    live_bytes = sum(x for x, _, _ in live)
+    live_gbs = live_bytes / (sum(live_ms) * 1e-3) / 1e9
+    spans = [(graph_t.timing[0][1].elapsed_time(a), graph_t.timing[0][1].elapsed_time(b))
+             for _, a, b in live]
+    for bt in batches:  # graph_t's warm-up leaves events the other graph must not wait on
+        for st in bt.layers:
+            st.ready = st.last_use = None
+
+    # ---- per-stage device time: the same number of steps run eagerly, one stage
+    # at a time (each micro-batch layer waits for the previous one, and its
+    # ready-row attention for its gather), with CUDA events on each launch's
+    # stream; a spin kernel ahead of every layer keeps the streams busy while the
+    # host enqueues, so no host gap lands inside a measured span
     timing = []
     eager_counts = [torch.zeros((steps, LAYERS, len(g), 3), dtype=torch.int64, device=device)
                     for g in groups]
     ref = torch.cuda.Event(enable_timing=True)
     ref.record(compute)
-    for bt in batches:
-        bt.compute.wait_event(ref)
+    prev = ref
     for s in range(warmup, total):
         for layer in range(LAYERS):
             for i, bt in enumerate(batches):
                 with torch.cuda.stream(bt.compute):
+                    bt.compute.wait_event(prev)
                     torch.cuda._sleep(1_000_000)
-                    bt.layer(layer, gq[i][s, layer], graph.outputs[i][layer],
-                             eager_counts[i][s - warmup, layer], timing)
+                    bt.layer(layer, gq[i][eager_base + s - warmup, layer], graph.outputs[i][layer],
+                             eager_counts[i][s - warmup, layer], timing, serial=True)
+                    prev = torch.cuda.Event()
+                    prev.record(bt.compute)
     for bt in batches:
         done = torch.cuda.Event()
         done.record(bt.compute)
@@ -375,10 +427,9 @@ def run_gpu(args, rank, world, local_rank, log):
 
     gather_busy_ms = union_ms(intervals["gather"])
     misses = int(timed_counts[..., 2].sum())
-    row_bytes = 2 * KV_HEADS * HEAD_DIM * 2
     gather_bytes = misses * row_bytes
-    # the eager pass repeats the timed steps' queries, but the hot buffer has
-    # moved on: its own miss bytes come from its own resolver counts
+    # the eager pass runs its own queries: its miss bytes come from its own
+    # resolver counts
     eager = np.concatenate([c.cpu().numpy() for c in eager_counts], axis=2)
     eager_gather_bytes = int(eager[..., 2].sum()) * row_bytes
     # micro-batches' gathers overlap on the one host link: the link's rate is
@@ -397,17 +448,19 @@ def run_gpu(args, rank, world, local_rank, log):
 
     # ---- end to end: queries copied in from pinned host memory and outputs read
     # back every step, through the same captured step ------------------------------
-    host_q = [g.cpu().pin_memory() for g in gq]
+    host_q = [g[e2e_base:].cpu().pin_memory() for g in gq]
     host_out = [torch.empty((total, *o.shape), dtype=DTYPE, pin_memory=True)
                 for o in graph.outputs]
+    e2e_counts = torch.zeros((total, LAYERS, REQUESTS, 3), dtype=torch.int64, device=device)
 
     def run_e2e(first, last):
         for s in range(first, last):
             for i in range(len(groups)):
-                graph.queries[i].copy_(host_q[i][s % total], non_blocking=True)
+                graph.queries[i].copy_(host_q[i][s], non_blocking=True)
             graph.replay()
-            for i in range(len(groups)):
-                host_out[i][s % total].copy_(graph.outputs[i], non_blocking=True)
+            for i, g in enumerate(groups):
+                host_out[i][s].copy_(graph.outputs[i], non_blocking=True)
+                e2e_counts[s, :, g] = graph.counts[i]
 
     run_e2e(0, warmup)
     barrier()
@@ -418,6 +471,7 @@ def run_gpu(args, rank, world, local_rank, log):
     e2e_end.record(compute)
     barrier()
     e2e_ms = max_over_ranks(e2e_start.elapsed_time(e2e_end))
+    e2e_misses = int(e2e_counts[warmup:, ..., 2].sum().item())
     flags = _lib.device_flags(device)
     if flags:
         raise RuntimeError(f"device flags raised during the bench: {flags}")
@@ -432,28 +486,36 @@ def run_gpu(args, rank, world, local_rank, log):
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic", "config": workload_config(),
         "e2e": {"value": round(tokens / (e2e_ms * 1e-3), 2), "unit": "tok/s",
-                "h2d_bytes_per_step": io_bytes, "d2h_bytes_per_step": io_bytes},
+                "h2d_bytes_per_step": io_bytes, "d2h_bytes_per_step": io_bytes,
+                "miss_rows_per_unit": round(e2e_misses / (steps * LAYERS * REQUESTS), 1)},
         # per layer and micro-batch: quest, resolve, gather, two attention phases
         # and the merge (replayed from one CUDA graph per step)
         "gpu_launches": int(6 * LAYERS * steps * len(batches)),
         "roofline": {
             "kernel": "gather_kernel (host->pool miss gather)", "bound": "hostlink",
-            "achieved": round(gather_gbs, 2),
-            "peak": round(link_peak, 2), "unit": "GB/s", "frac": round(gather_gbs / link_peak, 4),
+            "achieved": round(live_gbs, 2),
+            "peak": round(link_peak, 2), "unit": "GB/s", "frac": round(live_gbs / link_peak, 4),
             "peak_source": "measured in bench.py: pinned host->device cudaMemcpyAsync, 1 GiB",
-            "traffic": None,
-            "achieved_definition": "miss bytes / time any gather launch is running (CUDA events "
-                                   "on the transfer streams; the micro-batches' gathers share "
-                                   "the link)",
-            "bytes_per_launch": round(eager_gather_bytes / launches["gather"]),
-            "ms_per_launch": round(kernel_ms["gather"] / launches["gather"], 4),
-            "hostlink_busy_frac_eager": round(gather_busy_ms / prof_ms, 4),
+            "traffic": round(PCIE_READ_PER_GATHERED_BYTE * live_bytes / len(live)),
+            "traffic_definition": "PCIe read bytes per launch (ncu pcie__read_bytes.sum, scaled "
+                                  "from a one-layer capture by the bytes gathered)",
+            "achieved_definition": "miss rows x 4 KiB per launch / launch duration, CUDA events "
+                                   "around each gather on its transfer stream, captured in an "
+                                   "instrumented copy of the step graph replayed W+K steps "
+                                   "after the headline region; the last step's launches",
+            "instrumented_ms_per_step": round(roof_step_ms, 3),
+            "bytes_per_launch": round(live_bytes / len(live)),
+            "ms_per_launch": round(sum(live_ms) / len(live), 4),
+            "launches_timed": len(live),
+            "hostlink_busy_frac": round(union_ms(spans) / (max(e for _, e in spans) -
+                                                           min(s_ for s_, _ in spans)), 4),
+            "eager_pass_gbs": round(gather_gbs, 2),
         },
         "roofline_hbm": {
             "attend_kernels": {"achieved": round(attend_gbs, 1), "peak": hbm_peak,
                                "frac": round(attend_gbs / hbm_peak, 4), "unit": "GB/s",
                                "peak_source": hbm_source,
-                               "note": "ready-row phase runs concurrently with the gather",
+                               "note": "both attention phases, each timed alone",
                                "ms_per_launch": round(attend_ms / launches["attend_ready"], 4)},
             "quest_kernels": {"achieved": round(quest_gbs, 1), "peak": hbm_peak,
                               "frac": round(quest_gbs / hbm_peak, 4), "unit": "GB/s",
@@ -470,7 +532,8 @@ def run_gpu(args, rank, world, local_rank, log):
                      "hot_hits": int(timed_counts[..., 1].sum()), "misses": misses,
                      "miss_rows_per_unit": round(misses / (steps * LAYERS * REQUESTS), 1)},
         "kernel_ms_per_step": {k: round(v / steps, 3) for k, v in kernel_ms.items()},
-        "kernel_ms_note": "sums of launch durations over all micro-batches; launches overlap",
+        "kernel_ms_note": "per step, summed over micro-batches and layers; every stage timed "
+                          "alone in an eager pass (in the captured step they overlap)",
         "clocks": clocks,
     }
     return result

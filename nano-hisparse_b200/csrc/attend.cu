@@ -495,24 +495,31 @@ __global__ void __launch_bounds__(kMmaThreads, 1) attend_mma_kernel(AttendParams
 
 // Merge: one 128-thread CTA per (request, query head). Thread t reads the
 // (max, sum) of partial t (phase 0's splits, then phase 1's; at most
-// 2 * kMaxSplits = 128 partials), the block reduces the global max and the
-// denominator, and each thread then sums its output elements over the weighted
-// partials — three dependent steps instead of a serial walk over the splits.
+// 2 * kMaxSplits = 128 partials) and the block reduces the global max and the
+// denominator; then warp w accumulates the weighted partials w, w+4, ... (a lane
+// owns 4 consecutive output elements, float2 loads issued ahead of their use)
+// and the four warp sums are added in shared memory.
 constexpr int kMergeThreads = 2 * kMaxSplits;
+constexpr int kMergeWarps = kMergeThreads / 32;
 
 template <typename TQ>
 __global__ void __launch_bounds__(kMergeThreads) attend_merge_kernel(AttendParams p) {
   __shared__ float weight[kMergeThreads];
-  __shared__ float reduce[kMergeThreads / 32];
+  __shared__ float reduce[kMergeWarps];
   __shared__ float result[2];
+  __shared__ float acc_sm[kMergeWarps][128];
   const int h = blockIdx.x, b = blockIdx.y, t = threadIdx.x;
   const int lane = t & 31, warp = t >> 5;
-  const int D = p.head_dim;
+  const int D = p.head_dim, stride = D + 2;
+  const bool even = (D & 1) == 0;
   const int s0 = p.phase_splits[0], s1 = p.phases > 1 ? p.phase_splits[1] : 0;
   const int total = s0 + s1;
+  p.phase = 0;
+  const float *base0 = partial_slot(p, b, h, 0);
+  p.phase = 1;
+  const float *base1 = partial_slot(p, b, h, 0);
   auto partial = [&](int i) {
-    p.phase = i < s0 ? 0 : 1;
-    return partial_slot(p, b, h, i < s0 ? i : i - s0);
+    return i < s0 ? base0 + (int64_t)i * stride : base1 + (int64_t)(i - s0) * stride;
   };
   float m = -INFINITY, l = 0.f;
   if (t < total) {
@@ -525,7 +532,7 @@ __global__ void __launch_bounds__(kMergeThreads) attend_merge_kernel(AttendParam
   __syncthreads();
   if (t == 0) {
     float v = reduce[0];
-    for (int w = 1; w < kMergeThreads / 32; ++w) v = fmaxf(v, reduce[w]);
+    for (int w = 1; w < kMergeWarps; ++w) v = fmaxf(v, reduce[w]);
     result[0] = v;
   }
   __syncthreads();
@@ -538,20 +545,46 @@ __global__ void __launch_bounds__(kMergeThreads) attend_merge_kernel(AttendParam
   __syncthreads();
   if (t == 0) {
     float v = 0.f;
-    for (int i = 0; i < kMergeThreads / 32; ++i) v += reduce[i];
+    for (int i = 0; i < kMergeWarps; ++i) v += reduce[i];
     result[1] = v;
   }
   __syncthreads();
   const float denom = result[1];
   TQ *out = static_cast<TQ *>(p.out) + (int64_t)b * p.out_batch_stride + (int64_t)h * D;
-  for (int d = t; d < D; d += kMergeThreads) {
-    float num = 0.f;
+  for (int d0 = 0; d0 < D; d0 += 128) {
+    const int d = d0 + lane * 4;  // even D: partial rows are 8-byte aligned
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll 4
-    for (int i = 0; i < total; ++i) {
+    for (int i = warp; i < total; i += kMergeWarps) {
       const float wi = weight[i];
-      if (wi != 0.f) num += wi * partial(i)[d];
+      const float *src = partial(i) + d;
+      float2 v0 = make_float2(0.f, 0.f), v1 = make_float2(0.f, 0.f);
+      if (even && d + 3 < D) {
+        v0 = *reinterpret_cast<const float2 *>(src);
+        v1 = *reinterpret_cast<const float2 *>(src + 2);
+      } else {
+        if (d < D) v0.x = src[0];
+        if (d + 1 < D) v0.y = src[1];
+        if (d + 2 < D) v1.x = src[2];
+        if (d + 3 < D) v1.y = src[3];
+      }
+      if (wi != 0.f) {  // empty splits carry no weight
+        acc[0] += wi * v0.x;
+        acc[1] += wi * v0.y;
+        acc[2] += wi * v1.x;
+        acc[3] += wi * v1.y;
+      }
     }
-    out[d] = from_f32<TQ>(denom > 0.f ? num / denom : 0.f);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) acc_sm[warp][lane * 4 + k] = acc[k];
+    __syncthreads();
+    if (t < 128 && d0 + t < D) {
+      float num = 0.f;
+#pragma unroll
+      for (int w2 = 0; w2 < kMergeWarps; ++w2) num += acc_sm[w2][t];
+      out[d0 + t] = from_f32<TQ>(denom > 0.f ? num / denom : 0.f);
+    }
+    __syncthreads();
   }
 }
 

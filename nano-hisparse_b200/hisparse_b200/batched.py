@@ -58,8 +58,9 @@ class DecodeBatch:
                  q_heads, keep_sink=True, streams=None):
         """streams: optional (compute, transfer) CUDA streams for this batch; by
         default the cache's. Batches over disjoint requests with their own
-        streams run concurrently (micro-batch pipelining: one batch's gather
-        overlaps another's selection, resolve and attention)."""
+        compute streams run concurrently (micro-batch pipelining: one batch's
+        gather overlaps another's selection, resolve and attention); sharing one
+        transfer stream makes their gathers take the host link in turn."""
         self.cache, self.request_ids = cache, list(request_ids)
         if streams is None:
             self.compute, self.transfer = cache.compute, cache.transfer
@@ -99,14 +100,20 @@ class DecodeBatch:
         self.layers[layer].lengths.copy_(lengths)
 
     def layer(self, layer: int, query: torch.Tensor, out: torch.Tensor | None = None,
-              counts: torch.Tensor | None = None, timing: list | None = None) -> torch.Tensor:
+              counts: torch.Tensor | None = None, timing: list | None = None,
+              stages=None, serial: bool = False) -> torch.Tensor:
         """Hot path of `layer` for query [B, Hq, D] (CUDA, contiguous) on the
         cache's compute stream; returns attention output [B, Hq, D].
 
         counts: optional int64 [B, 3] CUDA tensor receiving the resolver counts
         (default: the layer's own buffer, see last_counts). timing: optional
         list; when given, (name, start, end) CUDA-event pairs recorded on each
-        launch's own stream are appended for the stages."""
+        launch's own stream are appended for the stages ("quest", "resolve",
+        "gather", "attend_ready", "attend_gathered", "merge"; all, or only those
+        in `stages`). The events are external, so they also time graph replays
+        when the call is captured. serial: run the ready-row attention after
+        the gather instead of beside it (each stage then runs alone, for
+        per-stage timing)."""
         cache, cfg, st, lib = self.cache, self.config, self.layers[layer], _lib.load()
         if torch.cuda.current_stream(self.device) != self.compute:
             raise RuntimeError("DecodeBatch.layer must run on the batch's compute stream")
@@ -123,23 +130,23 @@ class DecodeBatch:
         elif counts.shape != (b, 3) or counts.dtype != torch.int64 or not counts.is_contiguous():
             raise ValueError("counts must be a contiguous int64 [batch, 3] tensor")
 
-        def mark(stream_):
-            if timing is None:
+        def mark(stream_, *names):
+            if timing is None or (stages is not None and not any(n in stages for n in names)):
                 return None
-            event = torch.cuda.Event(enable_timing=True)
+            event = torch.cuda.Event(enable_timing=True, external=True)
             event.record(stream_)
             return event
 
         if st.ready is not None:
             compute.wait_event(st.ready)
-        t0 = mark(compute)
+        t0 = mark(compute, "quest")
         _lib.check(lib.hs_quest_select_batched(
             b, query.data_ptr(), hq * d, _lib.dtype_code(query.dtype), st.min_ptrs.data_ptr(),
             st.max_ptrs.data_ptr(), self._dtype, st.lengths.data_ptr(), hq, cfg.kv_heads, d,
             self.max_pages, cfg.page_size, self.top_pages, int(self.keep_sink),
             self.tokens.data_ptr(), self.width, self.token_counts.data_ptr(),
             _lib.ptr(self.quest_ws), self.quest_ws_bytes, status, stream))
-        t1 = mark(compute)
+        t1 = mark(compute, "quest", "resolve")
         _lib.check(lib.hs_resolve_rows_batched(
             b, self.tokens.data_ptr(), self.width, st.src_ptrs.data_ptr(), st.res_ptrs.data_ptr(),
             st.table_pages, st.hot_ptrs.data_ptr(), cache.hot_blocks, st.tag_ptrs.data_ptr(),
@@ -147,44 +154,50 @@ class DecodeBatch:
             self.physical.data_ptr(), self.miss_host.data_ptr(), self.miss_device.data_ptr(),
             counts.data_ptr(), self.ready.data_ptr(), _lib.ptr(self.resolve_ws),
             self.resolve_ws_bytes, status, stream))
-        t2 = mark(compute)
+        t2 = mark(compute, "resolve")
         resolved = torch.cuda.Event()
         resolved.record(compute)
         transfer.wait_event(resolved)
         if st.last_use is not None:
             transfer.wait_event(st.last_use)
-        t3 = mark(transfer)
+        t3 = mark(transfer, "gather")
         _lib.check(lib.hs_gather_rows(
             cache.mapped.data_ptr(), cache.host.shape[0], cache.pool.data_ptr(),
             cache.pool.shape[0], self.miss_host.data_ptr(), self.miss_device.data_ptr(),
             b * self.width, self.width, cfg.page_size, self._row_bytes, status,
             transfer.cuda_stream))
-        t4 = mark(transfer)
+        t4 = mark(transfer, "gather")
         st.ready = torch.cuda.Event()
         st.ready.record(transfer)
         # phase 0: rows that need no gather, concurrently with the gather
-        t5 = mark(compute)
+        if serial:
+            compute.wait_event(st.ready)
+        t5 = mark(compute, "attend_ready")
         common = (b, query.data_ptr(), hq * d, _lib.dtype_code(query.dtype), cache.pool.data_ptr(),
                   cache.pool.shape[0], self._dtype)
         _lib.check(lib.hs_attend_rows_phase(
             *common, self.ready.data_ptr(), self.width, self.width, counts.data_ptr(), 3, 0, 2, 0,
             hq, cfg.kv_heads, d, cfg.page_size, _lib.ptr(self.attend_ws), self.attend_ws_bytes,
             status, stream))
-        t6 = mark(compute)
+        t6 = mark(compute, "attend_ready")
         # phase 1: the gathered rows, then the merge
         compute.wait_event(st.ready)
-        t7 = mark(compute)
+        t7 = mark(compute, "attend_gathered")
         _lib.check(lib.hs_attend_rows_phase(
             *common, self.miss_device.data_ptr(), self.width, self.width, counts.data_ptr(), 3, 2,
             1, 1, hq, cfg.kv_heads, d, cfg.page_size, _lib.ptr(self.attend_ws),
             self.attend_ws_bytes, status, stream))
+        t8 = mark(compute, "attend_gathered", "merge")
         _lib.check(lib.hs_attend_merge(
             b, 2, out.data_ptr(), hq * d, _lib.dtype_code(query.dtype), hq, cfg.kv_heads, d,
             self.width, _lib.ptr(self.attend_ws), self.attend_ws_bytes, status, stream))
         if timing is not None:
-            t8 = mark(compute)
-            timing += [("quest", t0, t1), ("resolve", t1, t2), ("gather", t3, t4),
-                       ("attend_ready", t5, t6), ("attend_gathered", t7, t8)]
+            t9 = mark(compute, "merge")
+            for name, a, b_ in (("quest", t0, t1), ("resolve", t1, t2), ("gather", t3, t4),
+                                ("attend_ready", t5, t6), ("attend_gathered", t7, t8),
+                                ("merge", t8, t9)):
+                if a is not None and b_ is not None:
+                    timing.append((name, a, b_))
         st.last_use = torch.cuda.Event()
         st.last_use.record(compute)
         return out
@@ -210,7 +223,11 @@ class DecodeGraph:
     previous step's readers of its hot rows.
     """
 
-    def __init__(self, batches, layers: int, timing: bool = False):
+    def __init__(self, batches, layers: int, timing=False):
+        """timing: False, True (every stage) or an iterable of stage names of
+        DecodeBatch.layer; the captured step then records timing events, and
+        after a replay ``self.timing`` holds that replay's (name, start, end)
+        pairs for every (layer, batch)."""
         self.batches, self.layers = list(batches), layers
         b0 = self.batches[0]
         self.device = b0.device
@@ -221,6 +238,7 @@ class DecodeGraph:
         self.counts = [torch.zeros((layers, bt.batch, 3), dtype=torch.int64, device=self.device)
                        for bt in self.batches]
         self.timing = [] if timing else None
+        self.stages = None if timing is True or not timing else frozenset(timing)
         # two eager steps settle lazy state (function attributes, workspaces)
         # before capture; the events they leave behind are dropped
         for _ in range(2):
@@ -247,7 +265,7 @@ class DecodeGraph:
             for i, bt in enumerate(self.batches):
                 with torch.cuda.stream(bt.compute):
                     bt.layer(layer, self.queries[i][layer], self.outputs[i][layer],
-                             self.counts[i][layer], timing)
+                             self.counts[i][layer], timing, self.stages)
         for bt in self.batches:
             done = torch.cuda.Event()
             done.record(bt.compute)

@@ -189,7 +189,8 @@ def test_decode_graph_replay_matches_eager_steps():
         return out
 
     eager, captured = batches(caches[0]), batches(caches[1])
-    graph = DecodeGraph(captured, layers)  # runs two eager warm-up steps on caches[1]
+    # runs two eager warm-up steps on caches[1]; gather launches timed inside the graph
+    graph = DecodeGraph(captured, layers, timing=("gather",))
     gen = torch.Generator().manual_seed(11)
     warm = [torch.randn(layers, b, hq, d, generator=gen).to(torch.bfloat16) for _ in range(2)]
     steps = [torch.randn(layers, b, hq, d, generator=gen).to(torch.bfloat16) for _ in range(3)]
@@ -216,6 +217,8 @@ def test_decode_graph_replay_matches_eager_steps():
         torch.cuda.synchronize()
         for i, layer, out in ref:
             assert torch.equal(graph.outputs[i][layer], out)
+        assert len(graph.timing) == layers * len(groups)
+        assert all(name == "gather" and a.elapsed_time(b_) >= 0 for name, a, b_ in graph.timing)
     for key in caches[0].tables:
         assert torch.equal(caches[0].tables[key].tags, caches[1].tables[key].tags)
         assert torch.equal(caches[0].tables[key].lru, caches[1].tables[key].lru)
