@@ -656,6 +656,10 @@ def main():
 
         import torch.distributed as dist
 
+        # stdout carries exactly one JSON line: NCCL's own messages go to stderr
+        os.environ["NCCL_DEBUG"] = "WARN"
+        os.environ["NCCL_DEBUG_FILE"] = "/dev/stderr"
+
         torch.cuda.set_device(local_rank)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
                                 device_id=torch.device("cuda", local_rank))

@@ -9,7 +9,9 @@
  *   (3) the host->pool miss gather (nano_hisparse/row_kernels.py:35-70)
  *   (4) physical-row GQA decode attention (nano_hisparse/row_kernels.py:73-135,
  *       attention.py:26-35)
- * plus the mapped-host alias query (nano_hisparse/row_kernels.py:10-32).
+ * plus the mapped-host alias query (nano_hisparse/row_kernels.py:10-32) and
+ * the KV append that feeds (1): pool rows, host mirror and page metadata
+ * (nano_hisparse/storage.py:296-321).
  *
  * Conventions shared by every entry point:
  *   - Pointers are borrowed. The caller owns every buffer; the library never
@@ -252,6 +254,35 @@ HS_API int hs_attend_merge(int batch, int phases, void *out, int64_t out_batch_s
                            int query_dtype, int q_heads, int kv_heads, int head_dim,
                            int64_t count, void *workspace, size_t workspace_bytes,
                            int32_t *device_status, hs_stream stream);
+
+/* ---- (5) KV append: pool rows, host mirror, page metadata ---------------------
+ * Replaces the tensor work of HostStore.append (nano_hisparse/storage.py:
+ * 296-321) for one page chunk per batch item b with count[b] > 0:
+ *   rows within[b] .. within[b]+count[b]-1 of the K and V planes of pool block
+ *   pool_block[b] take rows 0 .. count[b]-1 of k and v (batch item b starts
+ *   kv_batch_stride elements after b-1; a row is kv_heads*head_dim elements);
+ *   when host_block[b] >= 0 the same rows of host block host_block[b] (through
+ *   host_alias, the hs_host_device_pointer alias) take the same values — the
+ *   host mirror, written by the kernel itself;
+ *   minimum_ptrs[b] / maximum_ptrs[b] point to the page's [kv_heads, head_dim]
+ *   bounds in the KV dtype: min/max of the new K rows folded in exactly as
+ *   torch.minimum(old, new) / torch.maximum(old, new) (NaN propagates, an equal
+ *   new value replaces the old);
+ *   summary_ptrs[b] points to the page's fp32 [kv_heads, head_dim] mean-K
+ *   summary: the K rows 0 .. within[b]+count[b]-1 of the block added in row
+ *   order in fp32, then divided by their number (bit-identical to the
+ *   reference's CPU mean).
+ * within/count are device int32[batch]; pool_block/host_block device
+ * int64[batch]; the pointer arrays device uint64[batch]. A chunk that leaves
+ * its page or addresses a block out of range is skipped and raises
+ * HS_DEV_ROW_OUT_OF_RANGE. Chunks of one launch must touch distinct pages. */
+HS_API int hs_append_rows(int batch, const void *k, const void *v, int64_t kv_batch_stride,
+                          int kv_dtype, const int32_t *within, const int32_t *count,
+                          const int64_t *pool_block, void *pool, int64_t pool_blocks,
+                          const int64_t *host_block, void *host_alias, int64_t host_blocks,
+                          const uint64_t *minimum_ptrs, const uint64_t *maximum_ptrs,
+                          const uint64_t *summary_ptrs, int kv_heads, int head_dim,
+                          int page_size, int32_t *device_status, hs_stream stream);
 
 /* hs_attend_rows without a caller workspace: no counterpart in the reference
  * (whose Triton attention needs no scratch). For callers with no device

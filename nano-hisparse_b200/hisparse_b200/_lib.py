@@ -54,6 +54,8 @@ _SIGNATURES = {
                               _INT, _INT, _INT, _INT, _INT, _INT, _INT, _P, _SZ, _P, _P], _INT),
     "hs_attend_merge": ([_INT, _INT, _P, _I64, _INT, _INT, _INT, _INT, _I64, _P, _SZ, _P, _P],
                         _INT),
+    "hs_append_rows": ([_INT, _P, _P, _I64, _INT, _P, _P, _P, _P, _I64, _P, _P, _I64, _P, _P,
+                        _P, _INT, _INT, _INT, _P, _P], _INT),
     "hs_attend_rows_static": ([_INT, _P, _I64, _INT, _P, _I64, _INT, _P, _I64, _I64, _I64, _P,
                                _I64, _INT, _INT, _INT, _INT, _P, _P], _INT),
 }

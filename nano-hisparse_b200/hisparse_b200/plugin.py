@@ -10,6 +10,7 @@ miss gather and row attention on the sm_100a kernels:
   nano_hisparse.hybrid.LogicalTopK                                  (hybrid.py:406-409)
   nano_hisparse.row_kernels.MappedHost / gather_rows / attend_rows  (hybrid.py:108-111,
                                                                      447-451; attention.py:22-25)
+  nano_hisparse.storage.HostStore.append                            (hybrid.py:391)
 
 The reference's residency policy, storage, model and engine are untouched.
 ``uninstall`` restores the original bindings.
@@ -20,6 +21,7 @@ from __future__ import annotations
 import importlib
 
 from . import row_kernels as _rk
+from .append import host_store_append
 from .row_index import LogicalTopK, resolve_rows
 from .selection import quest_selection
 
@@ -31,6 +33,7 @@ _BINDINGS = [
     ("row_kernels", "MappedHost", _rk.MappedHost),
     ("row_kernels", "gather_rows", _rk.gather_rows),
     ("row_kernels", "attend_rows", _rk.attend_rows),
+    ("storage", "HostStore.append", host_store_append),
 ]
 _saved: dict = {}
 
@@ -44,19 +47,29 @@ def install(package) -> list[str]:
     """
     done = []
     for module_name, attr, replacement in _BINDINGS:
-        module = importlib.import_module(f"{package.__name__}.{module_name}")
+        owner, name = _owner(package.__name__, module_name, attr)
         key = (package.__name__, module_name, attr)
         if key not in _saved:
-            _saved[key] = getattr(module, attr)
-        setattr(module, attr, replacement)
+            _saved[key] = owner.__dict__[name] if isinstance(owner, type) else getattr(owner,
+                                                                                       name)
+        setattr(owner, name, replacement)
         done.append(f"{module_name}.{attr}")
     return done
+
+
+def _owner(package_name, module_name, attr):
+    """The object holding `attr` ("name" in the module, or "Class.name")."""
+    owner = importlib.import_module(f"{package_name}.{module_name}")
+    *path, name = attr.split(".")
+    for part in path:
+        owner = getattr(owner, part)
+    return owner, name
 
 
 def uninstall(package) -> None:
     for (pkg, module_name, attr), original in list(_saved.items()):
         if pkg != package.__name__:
             continue
-        module = importlib.import_module(f"{pkg}.{module_name}")
-        setattr(module, attr, original)
+        owner, name = _owner(pkg, module_name, attr)
+        setattr(owner, name, original)
         del _saved[(pkg, module_name, attr)]

@@ -16,6 +16,9 @@
  *   or_resolve_rows   row_index.py:62-140  resolver + tag/LRU update
  *   or_gather_rows    hybrid.py:452-459    CPU gather loop (bytes)
  *   or_attend_rows    attention.py:26-35   masked softmax attention (fp64)
+ *   or_append_rows    storage.py:296-321   one page chunk of HostStore.append:
+ *                                          pool rows, host mirror, K min/max
+ *                                          and mean-K summary
  *
  * The Quest score is a fp32 sum whose order the reference leaves to torch.
  * This oracle fixes the order that libhisparse's kernel uses (stated in
@@ -405,6 +408,74 @@ int or_gather_rows(const uint8_t *host, int64_t host_blocks, uint8_t *pool, int6
     }
   }
   return rc;
+}
+
+/* ---- (5) append ---------------------------------------------------------------- */
+/*
+ * One page chunk of HostStore.append (storage.py:296-321): rows
+ * within .. within+count-1 of the K and V planes of `block` (one pool block,
+ * [2, P, E] elements, E = kv_heads*head_dim) take the count rows of k and v
+ * ([count, E]); `host_block` (NULL: no mirror) receives the same rows; then
+ *   minimum[e] = min(minimum[e], min_i k[i][e]) and maximum likewise — exact
+ *   in the KV dtype, NaN propagating, an equal new value replacing the old
+ *   (torch.minimum / torch.maximum of old and new);
+ *   summary[e] = (fp32) sum of K-plane rows 0 .. within+count-1, added in row
+ *   order, divided by within+count (the mean of storage.py:309).
+ * Element size is 4 (f32) or 2 (f16/bf16); min/max keep the winning element's
+ * bits, so no conversion back to the KV dtype is needed.
+ */
+static int elem_less(float a, float b) { return a < b; }
+
+int or_append_rows(const void *k, const void *v, int dtype, int64_t count, int64_t within,
+                   void *block, void *host_block, void *minimum, void *maximum,
+                   float *summary, int64_t elems, int P) {
+  if (count < 0 || within < 0 || within + count > P || elems < 1) return 1;
+  const int64_t es = dtype == OR_F32 ? 4 : 2;
+  uint8_t *blk = (uint8_t *)block;
+  const int64_t plane = (int64_t)P * elems * es, row = elems * es;
+  for (int64_t i = 0; i < count; ++i) {
+    memcpy(blk + (within + i) * row, (const uint8_t *)k + i * row, (size_t)row);
+    memcpy(blk + plane + (within + i) * row, (const uint8_t *)v + i * row, (size_t)row);
+    if (host_block) {
+      memcpy((uint8_t *)host_block + (within + i) * row, (const uint8_t *)k + i * row, (size_t)row);
+      memcpy((uint8_t *)host_block + plane + (within + i) * row, (const uint8_t *)v + i * row,
+             (size_t)row);
+    }
+  }
+  const int64_t valid = within + count;
+  for (int64_t e = 0; e < elems; ++e) {
+    if (count > 0) {
+      int64_t lo = 0, hi = 0, nan_row = -1; /* rows of the chunk holding the min / max */
+      for (int64_t i = 0; i < count; ++i) {
+        const float x = load_elem(k, dtype, i * elems + e);
+        if (isnan(x) && nan_row < 0) nan_row = i;
+        if (elem_less(x, load_elem(k, dtype, lo * elems + e))) lo = i;
+        if (elem_less(load_elem(k, dtype, hi * elems + e), x)) hi = i;
+      }
+      const float old_lo = load_elem(minimum, dtype, e), old_hi = load_elem(maximum, dtype, e);
+      const float new_lo = load_elem(k, dtype, lo * elems + e);
+      const float new_hi = load_elem(k, dtype, hi * elems + e);
+      uint8_t *const mn = (uint8_t *)minimum + e * es, *const mx = (uint8_t *)maximum + e * es;
+      const uint8_t *const kb = (const uint8_t *)k;
+      /* torch.minimum(old, new): NaN if either is NaN, else the smaller, the new one on ties */
+      if (isnan(old_lo)) {
+      } else if (nan_row >= 0) {
+        memcpy(mn, kb + (nan_row * elems + e) * es, (size_t)es);
+      } else if (!elem_less(old_lo, new_lo)) {
+        memcpy(mn, kb + (lo * elems + e) * es, (size_t)es);
+      }
+      if (isnan(old_hi)) {
+      } else if (nan_row >= 0) {
+        memcpy(mx, kb + (nan_row * elems + e) * es, (size_t)es);
+      } else if (!elem_less(new_hi, old_hi)) {
+        memcpy(mx, kb + (hi * elems + e) * es, (size_t)es);
+      }
+    }
+    float sum = 0.f;
+    for (int64_t r = 0; r < valid; ++r) sum += load_elem(blk, dtype, r * elems + e);
+    summary[e] = valid > 0 ? sum / (float)valid : 0.f;
+  }
+  return 0;
 }
 
 /* ---- (4) attention ------------------------------------------------------------- */

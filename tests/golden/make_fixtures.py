@@ -22,6 +22,8 @@ weights_only=True):
                       reference's own cache tests (test_hybrid.py,
                       test_residency.py) and trace replays (trace.py,
                       test_trace.py), with the final row counters
+  append_cases.pt     every HostStore.append (storage.py:296-321) of scripted
+                      prefill + decode sessions, with the state before/after
 """
 
 from __future__ import annotations
@@ -475,14 +477,103 @@ def scenarios(ref):
     return out
 
 
+# ---------------------------------------------------------------------------
+# append (metadata producer + host mirror)
+# ---------------------------------------------------------------------------
+def append_cases(ref):
+    """Every HostStore.append (storage.py:296-321) made by HybridKVCache.write
+    in scripted CPU sessions: prefill chunks spanning pages, then one-token
+    decode appends, for f32/f16/bf16 and several page sizes. Each record holds
+    the state of the written request/layer before and after the call and the
+    page chunks the call wrote (page index, offset, count, pool slot, host
+    slot, K/V rows)."""
+    from dataclasses import replace
+
+    import nano_hisparse.storage as storage_mod
+    from nano_hisparse.config import CacheConfig
+    from nano_hisparse.hybrid import HotConfig, HybridKVCache
+
+    original = storage_mod.HostStore.append
+    records = []
+
+    def recording_append(store, request_id, layer, k, v, prepare_page, after_write=None):
+        request = store.requests[request_id]
+        start = request.lengths[layer]
+        chunks = []
+
+        def prepare(page):
+            lease = prepare_page(page)
+            chunks.append({"index": page.key[2], "slot": int(page.slot),
+                           "host_slot": int(page.host_slot)})
+            return lease
+
+        pool_before, host_before = store.pool.clone(), store.host.clone()
+        meta_before = [t[layer].clone() for t in (request.minimum, request.maximum,
+                                                  request.summaries)]
+        result = original(store, request_id, layer, k, v, prepare, after_write)
+        offset = 0
+        for chunk in chunks:
+            position = start + offset
+            within = position % store.config.page_size
+            count = min(store.config.page_size - within, len(k) - offset)
+            index, slot, host_slot = chunk["index"], chunk["slot"], chunk["host_slot"]
+            # only the written page's block, host block and metadata entries
+            chunk.update(within=within, count=count, k=k[offset:offset + count].clone(),
+                         v=v[offset:offset + count].clone(),
+                         block_before=pool_before[slot].clone(),
+                         host_before=host_before[host_slot].clone(),
+                         block_after=store.pool[slot].clone(),
+                         host_after=store.host[host_slot].clone(),
+                         min_before=meta_before[0][index].clone(),
+                         max_before=meta_before[1][index].clone(),
+                         summary_before=meta_before[2][index].clone(),
+                         min_after=request.minimum[layer, index].clone(),
+                         max_after=request.maximum[layer, index].clone(),
+                         summary_after=request.summaries[layer, index].clone())
+            offset += count
+        records.append({"chunks": chunks, "page_size": store.config.page_size})
+        return result
+
+    storage_mod.HostStore.append = recording_append
+    out = []
+    try:
+        for ci, (dtype, page_size, heads, dim, prefill) in enumerate([
+                (torch.float32, 4, 2, 8, 10), (torch.float16, 8, 2, 16, 19),
+                (torch.bfloat16, 16, 4, 32, 37), (torch.bfloat16, 4, 1, 64, 4),
+                (torch.float16, 16, 8, 128, 16)]):
+            torch.manual_seed(300 + ci)
+            config = CacheConfig(gpu_pages=24, host_pages=128, page_size=page_size,
+                                 kv_heads=heads, head_dim=dim, device="cpu", dtype=dtype)
+            cache = HybridKVCache(config, HotConfig(2 * page_size, 2 * page_size))
+            cache.reserve("a", prefill + 24, 2)
+            for layer in range(2):
+                k, v = [torch.randn(prefill, heads, dim).to(dtype) for _ in range(2)]
+                cache.write("a", layer, k, v)
+            for _ in range(6):  # decode: one token per layer per step
+                for layer in range(2):
+                    k, v = [torch.randn(1, heads, dim).to(dtype) for _ in range(2)]
+                    cache.write("a", layer, k, v)
+            out.append({"name": f"append_{ci}_{str(dtype)[6:]}_P{page_size}",
+                        "records": records[:]})
+            records.clear()
+    finally:
+        storage_mod.HostStore.append = original
+    return out
+
+
 def main():
     parser = argparse.ArgumentParser(description=__doc__.split("\n\n")[0])
-    parser.add_argument("--reference", default="/root/reference")
+    parser.add_argument("--reference", required=True,
+                        help="path of a KiritoHugh/nano-hisparse checkout")
+    parser.add_argument("--only", nargs="*", help="fixture names to regenerate")
     args = parser.parse_args()
     ref = load_reference(args.reference)
     torch.set_num_threads(4)
     for name, fn in [("resolver_cases", resolver_cases), ("quest_cases", quest_cases),
-                     ("attention_cases", attention_cases), ("scenarios", scenarios)]:
+                     ("attention_cases", attention_cases), ("scenarios", scenarios),
+                     ("append_cases", append_cases)]:
+        if args.only and name not in args.only:
+            continue
         data = fn(ref)
         path = OUT / f"{name}.pt"
         torch.save(data, path)

@@ -72,7 +72,8 @@ def test_plugin_rebinds_and_restores_reference_names():
     originals = {}
     for sub, names in [("selection", ["quest_selection"]), ("model", ["quest_selection"]),
                        ("hybrid", ["resolve_rows", "LogicalTopK"]),
-                       ("row_kernels", ["MappedHost", "gather_rows", "attend_rows"])]:
+                       ("row_kernels", ["MappedHost", "gather_rows", "attend_rows"]),
+                       ("storage", [])]:
         mod = types.ModuleType(f"fake_reference.{sub}")
         for name in names:
             value = object()
@@ -80,11 +81,18 @@ def test_plugin_rebinds_and_restores_reference_names():
             originals[sub, name] = value
         sys.modules[mod.__name__] = mod
         setattr(pkg, sub, mod)
+    store_append = lambda self, *args: None  # noqa: E731
+    sys.modules["fake_reference.storage"].HostStore = type("HostStore", (),
+                                                           {"append": store_append})
     sys.modules["fake_reference"] = pkg
     try:
         bound = plugin.install(pkg)
-        assert len(bound) == 7
+        assert len(bound) == 8
         import hisparse_b200 as hs
+        from hisparse_b200.append import host_store_append
+
+        store_cls = sys.modules["fake_reference.storage"].HostStore
+        assert store_cls.append is host_store_append
 
         assert sys.modules["fake_reference.hybrid"].resolve_rows is hs.resolve_rows
         assert sys.modules["fake_reference.row_kernels"].attend_rows is hs.attend_rows
@@ -92,6 +100,7 @@ def test_plugin_rebinds_and_restores_reference_names():
         plugin.uninstall(pkg)
         for (sub, name), value in originals.items():
             assert getattr(sys.modules[f"fake_reference.{sub}"], name) is value
+        assert store_cls.__dict__["append"] is store_append
     finally:
         for key in [k for k in sys.modules if k.startswith("fake_reference")]:
             del sys.modules[key]

@@ -142,3 +142,25 @@ def test_oracle_gather_is_a_byte_copy(dtype):
     for h, d in ((0, 11), (17, 3), (5, 0)):
         expected[d // 3, :, d % 3] = host[h // 3, :, h % 3]
     assert same_bytes(pn, raw_numpy(expected))
+
+
+def test_oracle_append_matches_reference_fixtures(golden):
+    """The metadata producer + host mirror restatement reproduces every page
+    chunk HostStore.append wrote in the recorded sessions: pool block and
+    host block bytes, K min/max and the mean-K summary bit for bit."""
+    chunks = 0
+    for case in golden("append_cases"):
+        for record in case["records"]:
+            for c in record["chunks"]:
+                blk, host, mn, mx, summ = oracle.append_rows(
+                    c["k"], c["v"], c["within"], c["block_before"], c["host_before"],
+                    c["min_before"], c["max_before"], c["summary_before"].numpy())
+                assert np.array_equal(blk, oracle.as_array(c["block_after"])[0]), case["name"]
+                assert np.array_equal(host, oracle.as_array(c["host_after"])[0]), case["name"]
+                assert np.array_equal(mn, oracle.as_array(c["min_after"])[0]), case["name"]
+                assert np.array_equal(mx, oracle.as_array(c["max_after"])[0]), case["name"]
+                # rows added in order, then one division: torch's CPU mean gives
+                # the same fp32 bits on every recorded chunk
+                assert np.array_equal(summ, c["summary_after"].numpy()), case["name"]
+                chunks += 1
+    assert chunks > 60
