@@ -152,6 +152,43 @@ HS_API int hs_quest_select_batched(int batch, const void *query, int64_t query_b
                             size_t workspace_bytes, int32_t *device_status,
                             hs_stream stream);
 
+/* Head-sharded selection (configuration 5: one long request whose KV heads
+ * are split over ranks). Replaces quest_selection (selection.py:69-91) when
+ * each rank holds a slice of the heads: every rank runs
+ * hs_quest_partial_scores_batched on its slice, the ranks exchange the
+ * [batch, max_pages] partials (an all-gather), and every rank runs
+ * hs_quest_select_partials on all of them, which yields the same tokens on
+ * every rank.
+ *
+ * hs_quest_partial_scores_batched: arguments as hs_quest_select_batched for
+ * this rank's q_heads / kv_heads; out_partial [batch, max_pages] fp32
+ * receives, for pages p < ceil(length / page_size), the head sum of this
+ * slice in the fixed order above (the xor tree over lanes of the per-lane
+ * head sums, local head indices) WITHOUT the division by q_heads. Pages past
+ * a request's length are not written. Needs no workspace. */
+HS_API int hs_quest_partial_scores_batched(int batch, const void *query,
+                                           int64_t query_batch_stride, int query_dtype,
+                                           const uint64_t *minimum_ptrs,
+                                           const uint64_t *maximum_ptrs, int kv_dtype,
+                                           const int32_t *lengths, int q_heads, int kv_heads,
+                                           int head_dim, int64_t max_pages, int page_size,
+                                           float *out_partial, int32_t *device_status,
+                                           hs_stream stream);
+
+/* partials: [shards, batch, max_pages] fp32 (shard-major, as an all-gather
+ * leaves them). score_p = (((0 + partial[0][b][p]) + partial[1][b][p]) + ...)
+ * / q_heads (q_heads = the query heads of all shards), then the forced pages,
+ * top-k and expansion of hs_quest_select. With shards = 1 the tokens equal
+ * hs_quest_select's. Workspace: hs_quest_workspace_bytes(batch, max_pages),
+ * no initialisation needed. */
+HS_API int hs_quest_select_partials(int shards, const float *partials, int batch,
+                                    const int32_t *lengths, int q_heads, int64_t max_pages,
+                                    int page_size, int top_pages, int keep_sink,
+                                    int32_t *out_tokens, int64_t out_capacity,
+                                    int32_t *out_counts, void *workspace,
+                                    size_t workspace_bytes, int32_t *device_status,
+                                    hs_stream stream);
+
 /* ---- (2) row resolver ------------------------------------------------------
  * Replaces resolve_rows (nano_hisparse/row_index.py:62-140) with identical
  * results: physical rows in input order (duplicates after their first

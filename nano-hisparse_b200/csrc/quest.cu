@@ -45,8 +45,9 @@ template <typename TQ, typename TKV> struct QuestParams {
   int q_heads, kv_heads, head_dim, page_size, top_pages, keep_sink;
   int64_t max_pages;
   int tile_pages;  // pages per CTA (multiple of kPagesPerItem)
-  float *scores;   // workspace [batch, max_pages]
+  float *scores;   // workspace [batch, max_pages] (partial mode: the caller's output)
   unsigned *done;  // workspace [batch] completion counters (zero between calls)
+  int partial;     // 1: write head sums without the division and skip the selection
   int32_t *out_tokens;
   int64_t capacity;
   int32_t *out_counts;
@@ -337,9 +338,11 @@ __global__ void __launch_bounds__(kThreads, 2) quest_kernel(QuestParams<TQ, TKV>
       for (int h = lane; h < Hq; h += 32) u = __fadd_rn(u, head_sums[lp * Hq + h]);
       const float total = warp_xor_tree_sum(u);
       if (lane == 0)
-        p.scores[(int64_t)b * p.max_pages + tile0 + lp] = __fdiv_rn(total, (float)Hq);
+        p.scores[(int64_t)b * p.max_pages + tile0 + lp] =
+            p.partial ? total : __fdiv_rn(total, (float)Hq);
     }
   }
+  if (p.partial) return;  // shard of a head-sharded selection: no top-k here
   // completion: the last CTA of this request selects
   __threadfence();
   __syncthreads();
@@ -553,7 +556,7 @@ __global__ void __launch_bounds__(kTmaThreads, 1) quest_tma_kernel(QuestParams<T
         const float total = warp_xor_tree_sum(u);
         if (lane == 0)
           p.scores[(int64_t)b * p.max_pages + tile0 + (int64_t)g * kTmaStagePages + lp] =
-              __fdiv_rn(total, (float)Hq);
+              p.partial ? total : __fdiv_rn(total, (float)Hq);
       }
       if (!s_ok) {
         // a copy never completed: wait (bounded) for the stages still in
@@ -565,6 +568,7 @@ __global__ void __launch_bounds__(kTmaThreads, 1) quest_tma_kernel(QuestParams<T
     }
   }
 done:
+  if (p.partial) return;  // shard of a head-sharded selection: no top-k here
   __threadfence();
   __syncthreads();
   if (tid == 0) s_last = atomicAdd(&p.done[b], 1u) == gridDim.x - 1;
@@ -574,6 +578,57 @@ done:
   const int64_t cap_keys = (int64_t)(kTmaStages * stage_bytes / sizeof(uint32_t));
   select_request(p, b, length, n, n <= cap_keys ? reinterpret_cast<uint32_t *>(smem) : nullptr);
   if (tid == 0) p.done[b] = 0;
+}
+
+// Head-sharded selection, second half: the shards' per-page head sums are
+// added in shard order (left to right, fp32), divided by the total query
+// heads, and the usual top-k + expansion runs on the result — the same tokens
+// on every rank. With one shard this equals the unsharded selection bit for
+// bit (0 + s = s, and the same division).
+constexpr int kSelectThreads = 512;
+
+__global__ void __launch_bounds__(kSelectThreads)
+    select_partials_kernel(QuestParams<float, float> p, const float *partials, int shards) {
+  extern __shared__ uint32_t key_cache[];
+  const int b = blockIdx.x;
+  const int64_t length = p.lengths.at(b);
+  const int64_t n = length > 0 ? ceil_div(length, (int64_t)p.page_size) : 0;
+  float *sc = p.scores + (int64_t)b * p.max_pages;
+  if (n <= p.max_pages) {
+    for (int64_t pg = threadIdx.x; pg < n; pg += blockDim.x) {
+      float total = 0.f;
+      for (int r = 0; r < shards; ++r)
+        total = __fadd_rn(total, partials[((int64_t)r * p.batch + b) * p.max_pages + pg]);
+      sc[pg] = __fdiv_rn(total, (float)p.q_heads);
+    }
+  }
+  __syncthreads();
+  select_request(p, b, length, n, n <= kSmemKeys ? key_cache : nullptr);
+}
+
+int launch_select_partials(int shards, const float *partials, int batch, const int32_t *lengths,
+                           int q_heads, int64_t max_pages, int page_size, int top_pages,
+                           int keep_sink, int32_t *out_tokens, int64_t capacity,
+                           int32_t *out_counts, float *scores, int32_t *status,
+                           cudaStream_t stream) {
+  QuestParams<float, float> p{};
+  p.batch = batch;
+  p.lengths = Lengths{lengths, 0};
+  p.q_heads = q_heads;
+  p.page_size = page_size;
+  p.top_pages = top_pages;
+  p.keep_sink = keep_sink;
+  p.max_pages = max_pages;
+  p.scores = scores;
+  p.out_tokens = out_tokens;
+  p.capacity = capacity;
+  p.out_counts = out_counts;
+  p.status = status;
+  const size_t smem = (size_t)(max_pages < kSmemKeys ? max_pages : kSmemKeys) * sizeof(uint32_t);
+  const int rc = reserve_smem((const void *)select_partials_kernel, smem, "quest select");
+  if (rc != HS_OK) return rc;
+  select_partials_kernel<<<batch, kSelectThreads, smem, stream>>>(p, partials, shards);
+  return check_launch("select_partials_kernel");
 }
 
 int tile_pages_for(int batch, int64_t max_pages) {
@@ -681,6 +736,7 @@ struct Common {
   void *workspace;
   size_t workspace_bytes;
   int32_t *status;
+  float *partial_out;  // head-sharded selection: per-page head sums of this shard
 };
 
 template <typename TQ, typename TKV> int run(const Common &c, cudaStream_t stream) {
@@ -697,9 +753,16 @@ template <typename TQ, typename TKV> int run(const Common &c, cudaStream_t strea
   p.top_pages = c.top_pages;
   p.keep_sink = c.keep_sink;
   p.max_pages = c.max_pages;
-  p.scores = static_cast<float *>(c.workspace);
-  p.done = reinterpret_cast<unsigned *>(static_cast<char *>(c.workspace) +
-                                        (size_t)c.batch * c.max_pages * sizeof(float));
+  if (c.partial_out != nullptr) {
+    p.scores = c.partial_out;
+    p.done = nullptr;
+    p.partial = 1;
+  } else {
+    p.scores = static_cast<float *>(c.workspace);
+    p.done = reinterpret_cast<unsigned *>(static_cast<char *>(c.workspace) +
+                                          (size_t)c.batch * c.max_pages * sizeof(float));
+    p.partial = 0;
+  }
   p.out_tokens = c.out_tokens;
   p.capacity = c.capacity;
   p.out_counts = c.out_counts;
@@ -724,15 +787,19 @@ int quest_common(const Common &c, cudaStream_t stream) {
   if (c.batch < 1 || c.q_heads < 1 || c.kv_heads < 1 || c.head_dim < 1 || c.page_size < 1 ||
       c.max_pages < 1)
     return set_error(HS_ERR_INVALID_ARGUMENT, "quest: dimensions must be positive");
-  if (c.top_pages < 1 || c.q_heads % c.kv_heads)
+  const bool partial = c.partial_out != nullptr;
+  if ((!partial && c.top_pages < 1) || c.q_heads % c.kv_heads)
     return set_error(HS_ERR_INVALID_ARGUMENT, "invalid page budget or GQA shape");
   if (c.head_dim > 256)
     return set_error(HS_ERR_UNSUPPORTED, "quest: head_dim %d > 256 is not supported",
                      c.head_dim);
-  if (!c.query || !c.out_tokens || !c.out_counts || (!c.mn && !c.mn_ptrs) ||
+  if (!c.query || (!partial && (!c.out_tokens || !c.out_counts)) || (!c.mn && !c.mn_ptrs) ||
       (!c.mx && !c.mx_ptrs))
     return set_error(HS_ERR_INVALID_ARGUMENT, "quest: null tensor pointer");
-  if (c.capacity < (int64_t)c.top_pages * c.page_size)
+  if (partial) {
+    if (c.max_pages * (int64_t)c.page_size > INT32_MAX)
+      return set_error(HS_ERR_INVALID_ARGUMENT, "quest: token positions must fit int32");
+  } else if (c.capacity < (int64_t)c.top_pages * c.page_size)
     return set_error(HS_ERR_INVALID_ARGUMENT,
                      "quest: out_capacity %lld < top_pages * page_size = %lld",
                      (long long)c.capacity, (long long)c.top_pages * c.page_size);
@@ -742,7 +809,7 @@ int quest_common(const Common &c, cudaStream_t stream) {
     return set_error(HS_ERR_UNSUPPORTED, "quest: %d query heads do not fit shared memory",
                      c.q_heads);
   const size_t need = hs_quest_workspace_bytes(c.batch, c.max_pages);
-  if (!c.workspace || c.workspace_bytes < need)
+  if (!partial && (!c.workspace || c.workspace_bytes < need))
     return set_error(HS_ERR_WORKSPACE, "quest: workspace of %zu bytes < required %zu",
                      c.workspace_bytes, need);
   switch (c.query_dtype) {
@@ -779,7 +846,7 @@ extern "C" int hs_quest_select(const void *query, int query_dtype, const void *m
   hs::Common c{1, query, 0, query_dtype, minimum, maximum, nullptr, nullptr, kv_dtype,
                hs::Lengths{nullptr, length}, q_heads, kv_heads, head_dim, page_size,
                top_pages, keep_sink, max_pages, out_tokens, out_capacity, out_count,
-               workspace, workspace_bytes, device_status};
+               workspace, workspace_bytes, device_status, nullptr};
   return hs::quest_common(c, static_cast<cudaStream_t>(stream));
 }
 
@@ -798,6 +865,51 @@ extern "C" int hs_quest_select_batched(int batch, const void *query,
   hs::Common c{batch, query, query_batch_stride, query_dtype, nullptr, nullptr, minimum_ptrs,
                maximum_ptrs, kv_dtype, hs::Lengths{lengths, 0}, q_heads, kv_heads, head_dim,
                page_size, top_pages, keep_sink, max_pages, out_tokens, out_capacity,
-               out_counts, workspace, workspace_bytes, device_status};
+               out_counts, workspace, workspace_bytes, device_status, nullptr};
   return hs::quest_common(c, static_cast<cudaStream_t>(stream));
+}
+
+// ---- head-sharded selection (a request's KV heads split over ranks) -------------
+extern "C" int hs_quest_partial_scores_batched(
+    int batch, const void *query, int64_t query_batch_stride, int query_dtype,
+    const uint64_t *minimum_ptrs, const uint64_t *maximum_ptrs, int kv_dtype,
+    const int32_t *lengths, int q_heads, int kv_heads, int head_dim, int64_t max_pages,
+    int page_size, float *out_partial, int32_t *device_status, hs_stream stream) {
+  if (!minimum_ptrs || !maximum_ptrs || !lengths || !out_partial)
+    return hs::set_error(HS_ERR_INVALID_ARGUMENT, "quest: null pointer array or output");
+  hs::Common c{batch, query, query_batch_stride, query_dtype, nullptr, nullptr, minimum_ptrs,
+               maximum_ptrs, kv_dtype, hs::Lengths{lengths, 0}, q_heads, kv_heads, head_dim,
+               page_size, 1, 0, max_pages, nullptr, 0, nullptr, nullptr, 0, device_status,
+               out_partial};
+  return hs::quest_common(c, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int hs_quest_select_partials(int shards, const float *partials, int batch,
+                                        const int32_t *lengths, int q_heads, int64_t max_pages,
+                                        int page_size, int top_pages, int keep_sink,
+                                        int32_t *out_tokens, int64_t out_capacity,
+                                        int32_t *out_counts, void *workspace,
+                                        size_t workspace_bytes, int32_t *device_status,
+                                        hs_stream stream) {
+  using namespace hs;
+  if (shards < 1 || batch < 1 || q_heads < 1 || max_pages < 1 || page_size < 1 ||
+      top_pages < 1)
+    return set_error(HS_ERR_INVALID_ARGUMENT, "quest: dimensions must be positive");
+  if (batch > 65535) return set_error(HS_ERR_UNSUPPORTED, "quest: batch %d > 65535", batch);
+  if (!partials || !lengths || !out_tokens || !out_counts)
+    return set_error(HS_ERR_INVALID_ARGUMENT, "quest: null tensor pointer");
+  if (out_capacity < (int64_t)top_pages * page_size)
+    return set_error(HS_ERR_INVALID_ARGUMENT,
+                     "quest: out_capacity %lld < top_pages * page_size = %lld",
+                     (long long)out_capacity, (long long)top_pages * page_size);
+  if (out_capacity > INT32_MAX || max_pages * (int64_t)page_size > INT32_MAX)
+    return set_error(HS_ERR_INVALID_ARGUMENT, "quest: token positions must fit int32");
+  const size_t need = hs_quest_workspace_bytes(batch, max_pages);
+  if (!workspace || workspace_bytes < need)
+    return set_error(HS_ERR_WORKSPACE, "quest: workspace of %zu bytes < required %zu",
+                     workspace_bytes, need);
+  return launch_select_partials(shards, partials, batch, lengths, q_heads, max_pages,
+                                page_size, top_pages, keep_sink, out_tokens, out_capacity,
+                                out_counts, static_cast<float *>(workspace), device_status,
+                                static_cast<cudaStream_t>(stream));
 }

@@ -41,6 +41,10 @@ _SIGNATURES = {
                          _INT, _P, _I64, _P, _P, _SZ, _P, _P], _INT),
     "hs_quest_select_batched": ([_INT, _P, _I64, _INT, _P, _P, _INT, _P, _INT, _INT, _INT, _I64,
                                  _INT, _INT, _INT, _P, _I64, _P, _P, _SZ, _P, _P], _INT),
+    "hs_quest_partial_scores_batched": ([_INT, _P, _I64, _INT, _P, _P, _INT, _P, _INT, _INT,
+                                         _INT, _I64, _INT, _P, _P, _P], _INT),
+    "hs_quest_select_partials": ([_INT, _P, _INT, _P, _INT, _I64, _INT, _INT, _INT, _P, _I64,
+                                  _P, _P, _SZ, _P, _P], _INT),
     "hs_resolve_workspace_bytes": ([_INT, _I64, _I64], _SZ),
     "hs_resolve_rows": ([_P, _INT, _I64, _P, _P, _I64, _P, _I64, _P, _P, _I64, _I64, _INT, _P,
                          _P, _P, _P, _P, _I64, _I64, _P, _P, _SZ, _P, _P], _INT),

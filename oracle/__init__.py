@@ -41,6 +41,7 @@ def lib():
         _lib = ctypes.CDLL(str(LIB_PATH))
         _lib.or_quest_scores.argtypes = [_P, _INT, _P, _P, _INT, _INT, _INT, _INT, _I64, _P]
         _lib.or_quest_select.argtypes = [_P, _I64, _INT, _INT, _INT, _P, _I64, _P]
+        _lib.or_quest_head_sums.argtypes = [_P, _INT, _P, _P, _INT, _INT, _INT, _INT, _I64, _P]
         _lib.or_resolve_rows.argtypes = [_P, _I64, _P, _P, _I64, _P, _I64, _P, _P, _I64, _I64,
                                          _INT, _P, _P, _P, _P]
         _lib.or_gather_rows.argtypes = [_P, _I64, _P, _I64, _P, _P, _I64, _INT, _I64]
@@ -52,7 +53,8 @@ def lib():
         _lib.or_append_rows.argtypes = [_P, _P, _INT, _I64, _I64, _P, _P, _P, _P, _P, _I64,
                                         _INT]
         for name in ("or_quest_scores", "or_quest_select", "or_resolve_rows", "or_gather_rows",
-                     "or_attend_rows", "or_decode_layer_batched", "or_append_rows"):
+                     "or_attend_rows", "or_decode_layer_batched", "or_append_rows",
+                     "or_quest_head_sums"):
             getattr(_lib, name).restype = _INT
     return _lib
 
@@ -94,6 +96,33 @@ def quest_scores(query, minimum, maximum, pages):
     if rc:
         raise ValueError(f"or_quest_scores failed: {rc}")
     return out
+
+
+def quest_sharded_scores(query, minimum, maximum, pages, shards):
+    """Scores of a head-sharded selection: shard r holds KV heads
+    [r*Hkv/W, (r+1)*Hkv/W) and their query heads; its undivided head sums are
+    added in shard order in float32, then divided by Hq (with shards = 1 this
+    equals quest_scores bit for bit)."""
+    q, qd = as_array(query)
+    mn, kd = as_array(minimum)
+    mx, _ = as_array(maximum)
+    hq, d = q.shape
+    hkv = mn.shape[1]
+    if hkv % shards:
+        raise ValueError("KV heads must split evenly over the shards")
+    kl, ql = hkv // shards, hq // shards
+    total = np.zeros(pages, dtype=np.float32)
+    for r in range(shards):
+        qs = np.ascontiguousarray(q[r * ql:(r + 1) * ql])
+        ms = np.ascontiguousarray(mn[:pages, r * kl:(r + 1) * kl])
+        xs = np.ascontiguousarray(mx[:pages, r * kl:(r + 1) * kl])
+        part = np.empty(pages, dtype=np.float32)
+        rc = lib().or_quest_head_sums(_ptr(qs), qd, _ptr(ms), _ptr(xs), kd, ql, kl, d, pages,
+                                      _ptr(part))
+        if rc:
+            raise ValueError(f"or_quest_head_sums failed: {rc}")
+        total = total + part
+    return total / np.float32(hq)
 
 
 def quest_select(scores, length, page_size, top_pages, keep_sink=True, capacity=None):

@@ -11,6 +11,8 @@
  * semantics, not transcribed from the reference's tensor programs:
  *
  *   or_quest_scores   selection.py:69-91   Quest upper bound, head mean
+ *   or_quest_head_sums                     the same, undivided, for one shard
+ *                                          of a head-sharded selection
  *   or_quest_select   selection.py:86-91   forced tail/sink, top-k, and
  *                     selection.py:45-62   page -> token expansion
  *   or_resolve_rows   row_index.py:62-140  resolver + tag/LRU update
@@ -81,9 +83,11 @@ static float xor_tree32(float x[32]) {
 }
 
 /* ---- (1) Quest scores --------------------------------------------------- */
-/* q: [Hq, D] (qdtype); mn/mx: [>= n, Hkv, D] (kvdtype); scores: [n]. */
-int or_quest_scores(const void *q, int qdtype, const void *mn, const void *mx, int kvdtype,
-                    int Hq, int Hkv, int D, int64_t n, float *scores) {
+/* q: [Hq, D] (qdtype); mn/mx: [>= n, Hkv, D] (kvdtype); scores: [n].
+ * divide = 0 leaves the head sum undivided: the partial score of one shard of a
+ * head-sharded selection (heads indexed locally, same order). */
+static int quest_scores(const void *q, int qdtype, const void *mn, const void *mx, int kvdtype,
+                        int Hq, int Hkv, int D, int64_t n, float *scores, int divide) {
   if (Hq < 1 || Hkv < 1 || D < 1 || Hq % Hkv) return 1;
   const int g = Hq / Hkv, C = (D + 31) / 32;
   float *qf = (float *)malloc(sizeof(float) * (size_t)Hq * D);
@@ -121,13 +125,25 @@ int or_quest_scores(const void *q, int qdtype, const void *mn, const void *mx, i
     /* lane j adds heads j, j+32, ... left to right; lanes meet in the xor tree */
     float u[32] = {0};
     for (int h = 0; h < Hq; ++h) u[h % 32] = u[h % 32] + s[h];
-    scores[p] = xor_tree32(u) / (float)Hq;
+    scores[p] = divide ? xor_tree32(u) / (float)Hq : xor_tree32(u);
   }
   free(qf);
   free(s);
   free(lo);
   free(hi);
   return 0;
+}
+
+int or_quest_scores(const void *q, int qdtype, const void *mn, const void *mx, int kvdtype,
+                    int Hq, int Hkv, int D, int64_t n, float *scores) {
+  return quest_scores(q, qdtype, mn, mx, kvdtype, Hq, Hkv, D, n, scores, 1);
+}
+
+/* Head sums of one shard (hs_quest_partial_scores_batched); the shards' sums
+ * are added in shard order and divided by the total heads by the caller. */
+int or_quest_head_sums(const void *q, int qdtype, const void *mn, const void *mx, int kvdtype,
+                       int Hq, int Hkv, int D, int64_t n, float *sums) {
+  return quest_scores(q, qdtype, mn, mx, kvdtype, Hq, Hkv, D, n, sums, 0);
 }
 
 /* ---- (1) forced pages, top-k and token expansion -------------------------- */

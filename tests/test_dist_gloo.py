@@ -42,3 +42,47 @@ def test_two_ranks_shard_and_reduce():
     mp.start_processes(_worker, args=(world, _free_port(), out), nprocs=world,
                        start_method="spawn", join=True)
     assert dict(out) == {0: (True, 11.0), 1: (True, 11.0)}
+
+
+def _sharded_worker(rank, world, port, out):
+    import sys
+    from pathlib import Path
+
+    import numpy as np
+
+    root = Path(__file__).resolve().parent.parent
+    sys.path.insert(0, str(root / "nano-hisparse_b200"))
+    sys.path.insert(0, str(root))
+    import oracle
+    from hisparse_b200.sharded import head_slice
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        gen = torch.Generator().manual_seed(3)
+        hq, hkv, d, p, length, top = 8, 4, 32, 16, 4000, 12
+        pages = -(-length // p)
+        q = torch.randn(hq, d, generator=gen)
+        keys = torch.randn(pages, 4, hkv, d, generator=gen)
+        mn, mx = keys.amin(1), keys.amax(1)
+        ks, qs = head_slice(hkv, hq, rank, world)
+        # this rank's undivided head sums (the oracle stands in for the kernel)
+        part = oracle.quest_sharded_scores(q[qs], mn[:, ks], mx[:, ks], pages, 1) * np.float32(
+            hq // world)
+        mine = torch.from_numpy(part)
+        gathered = [torch.empty_like(mine) for _ in range(world)]
+        dist.all_gather(gathered, mine)
+        out[rank] = [t.numpy().tobytes() for t in gathered]
+    finally:
+        dist.destroy_process_group()
+
+
+def test_two_ranks_exchange_partial_scores_in_rank_order():
+    """Head-sharded selection's exchange: every rank ends with the partials of
+    all ranks in rank order (the bytes the shared top-k is computed from)."""
+    world = 2
+    manager = mp.get_context("spawn").Manager()
+    out = manager.dict()
+    mp.start_processes(_sharded_worker, args=(world, _free_port(), out), nprocs=world,
+                       start_method="spawn", join=True)
+    assert out[0] == out[1] and len(out[0]) == world and out[0][0] != out[0][1]

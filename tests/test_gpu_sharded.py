@@ -1,0 +1,169 @@
+"""Head-sharded Quest selection (configuration 5): per-shard partial scores,
+the shard-ordered combine and the shared top-k, vs the unsharded kernel, the
+oracle's restatement of the sharded order and the reference's selections."""
+
+import math
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from helpers import quest_sets_agree
+from hisparse_b200 import _lib, quest_selection
+from hisparse_b200.sharded import head_slice, sharded_quest_selection
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda:0"
+
+
+def _emulated(q, mn, mx, length, page_size, top_pages, keep_sink, shards):
+    """W shards run one after another on one GPU: partials, stack, select."""
+    lib = _lib.load()
+    hq, hkv = q.shape[0], mn.shape[1]
+    max_pages = mn.shape[0]
+    lengths = torch.tensor([length], dtype=torch.int32, device=DEV)
+    partials = torch.empty((shards, max_pages), dtype=torch.float32, device=DEV)
+    status, stream = _lib.status_word(DEV).data_ptr(), _lib.stream_of(DEV)
+    for r in range(shards):
+        ks, qs = head_slice(hkv, hq, r, shards)
+        qr = q[qs].contiguous()
+        mr, xr = mn[:, ks].contiguous(), mx[:, ks].contiguous()
+        ptrs = torch.tensor([mr.data_ptr(), xr.data_ptr()], dtype=torch.int64, device=DEV)
+        _lib.check(lib.hs_quest_partial_scores_batched(
+            1, qr.data_ptr(), 0, _lib.dtype_code(qr.dtype), ptrs[0:1].data_ptr(),
+            ptrs[1:2].data_ptr(), _lib.dtype_code(mr.dtype), lengths.data_ptr(), qr.shape[0],
+            mr.shape[1], qr.shape[1], max_pages, page_size, partials[r].data_ptr(), status,
+            stream))
+        torch.cuda.synchronize()  # mr/xr/ptrs are freed at the end of the iteration
+    width = top_pages * page_size
+    tokens = torch.empty(width, dtype=torch.int32, device=DEV)
+    count = torch.empty(1, dtype=torch.int32, device=DEV)
+    nbytes = lib.hs_quest_workspace_bytes(1, max_pages)
+    ws = torch.empty(nbytes, dtype=torch.uint8, device=DEV)
+    _lib.check(lib.hs_quest_select_partials(
+        shards, partials.data_ptr(), 1, lengths.data_ptr(), hq, max_pages, page_size,
+        top_pages, int(keep_sink), tokens.data_ptr(), width, count.data_ptr(), ws.data_ptr(),
+        nbytes, status, stream))
+    torch.cuda.synchronize()
+    return [t for t in tokens.tolist()[:int(count.item())]], partials
+
+
+def _metadata(gen, pages, hkv, d, dtype):
+    keys = torch.randn(pages, 4, hkv, d, generator=gen).to(dtype)
+    return keys.float().amin(1).to(dtype), keys.float().amax(1).to(dtype)
+
+
+def test_one_shard_equals_unsharded_selection():
+    gen = torch.Generator().manual_seed(5)
+    for hq, hkv, d, p, length, top, dtype in [(32, 8, 128, 16, 32768, 128, torch.bfloat16),
+                                              (8, 2, 32, 16, 150, 4, torch.float32),
+                                              (6, 2, 24, 7, 1000, 9, torch.float16)]:
+        pages = math.ceil(length / p)
+        q = torch.randn(hq, d, generator=gen).to(dtype).to(DEV)
+        mn, mx = (t.to(DEV) for t in _metadata(gen, pages, hkv, d, dtype))
+        for sink in (True, False):
+            ref = quest_selection(q, mn, mx, length, p, top, sink)
+            got = sharded_quest_selection(q, mn, mx, length, p, top, sink)
+            assert torch.equal(ref.device_tokens, got.device_tokens)
+    assert not _lib.device_flags(DEV)
+
+
+@pytest.mark.parametrize("shards", [2, 4])
+@pytest.mark.parametrize("hq,hkv,d,p,length,top,dtype", [
+    (28, 4, 128, 64, 1048576, 128, torch.bfloat16),   # configuration 5
+    (32, 8, 128, 16, 32768, 128, torch.bfloat16),
+    (8, 4, 64, 16, 5000, 17, torch.float16),
+])
+def test_emulated_shards_match_oracle(shards, hq, hkv, d, p, length, top, dtype):
+    if hkv % shards:
+        pytest.skip("KV heads do not split evenly")
+    gen = torch.Generator().manual_seed(6 + shards)
+    pages = math.ceil(length / p)
+    q = torch.randn(hq, d, generator=gen).to(dtype)
+    mn, mx = _metadata(gen, pages, hkv, d, dtype)
+    got, partials = _emulated(q.to(DEV), mn.to(DEV), mx.to(DEV), length, p, top, True, shards)
+    scores = oracle.quest_sharded_scores(q, mn, mx, pages, shards)
+    tokens, count = oracle.quest_select(scores, length, p, top, True)
+    assert got == tokens[:count].tolist()
+    # each shard's partial is the oracle's undivided head sum of its slice
+    ks, qs = head_slice(hkv, hq, shards - 1, shards)
+    part = oracle.quest_sharded_scores(q[qs], mn[:, ks], mx[:, ks], pages, 1) * np.float32(
+        hq // shards)
+    np.testing.assert_allclose(partials[-1, :pages].cpu().numpy(), part, rtol=1e-6, atol=1e-6)
+    assert not _lib.device_flags(DEV)
+
+
+def test_sharded_selection_agrees_with_reference(golden):
+    """The reference averages over all heads in torch's order; the sharded sum
+    may differ from it only at near-ties of the k-th score."""
+    checked = 0
+    for case in golden("quest_cases"):
+        hq, hkv = case["query"].shape[0], case["minimum"].shape[1]
+        if hkv % 2 or "tokens_1" not in case:
+            continue
+        q, mn, mx = (case[k].to(DEV) for k in ("query", "minimum", "maximum"))
+        got, _ = _emulated(q, mn, mx, case["length"], case["page_size"], case["top_pages"],
+                           True, 2)
+        pages = math.ceil(case["length"] / case["page_size"])
+        if case["top_pages"] >= pages:
+            continue
+        ok, detail = quest_sets_agree(case["tokens_1"], got, case["query"], case["minimum"],
+                                      case["maximum"], case["length"], case["page_size"],
+                                      case["top_pages"], True)
+        assert ok, f"{case['name']}: {detail}"
+        checked += 1
+    assert checked >= 5
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _rank(rank, world, port, q, mn, mx, length, p, top, out):
+    import sys
+    from pathlib import Path
+
+    root = Path(__file__).resolve().parent.parent
+    sys.path.insert(0, str(root / "nano-hisparse_b200"))
+    import datetime
+
+    import torch.distributed as dist
+
+    from hisparse_b200.sharded import head_slice as hs_slice
+    from hisparse_b200.sharded import sharded_quest_selection as sqs
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60), device_id=dev)
+    try:
+        ks, qs = hs_slice(mn.shape[1], q.shape[0], rank, world)
+        sel = sqs(q[qs].to(dev), mn[:, ks].contiguous().to(dev), mx[:, ks].contiguous().to(dev),
+                  length, p, top)
+        out[rank] = sel.device_tokens.cpu().tolist()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_two_ranks_over_nccl_agree_with_emulation():
+    import torch.multiprocessing as mp
+
+    gen = torch.Generator().manual_seed(9)
+    hq, hkv, d, p, length, top = 28, 4, 128, 64, 262144, 128
+    pages = math.ceil(length / p)
+    q = torch.randn(hq, d, generator=gen).to(torch.bfloat16)
+    mn, mx = _metadata(gen, pages, hkv, d, torch.bfloat16)
+    expected, _ = _emulated(q.to(DEV), mn.to(DEV), mx.to(DEV), length, p, top, True, 2)
+    manager = mp.get_context("spawn").Manager()
+    out = manager.dict()
+    mp.start_processes(_rank, args=(2, _free_port(), q, mn, mx, length, p, top, out), nprocs=2,
+                       start_method="spawn", join=True)
+    for rank in range(2):
+        assert [t for t in out[rank] if t >= 0] == expected
