@@ -84,12 +84,15 @@ def measured_peaks():
 # clocks
 # ---------------------------------------------------------------------------
 class ClockSampler:
-    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+    """nvidia-smi clock/throttle samples every 50 ms, kept for the timed window."""
+
+    QUERY = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
     def __init__(self, index):
         self.index, self.proc, self.path = index, None, None
+        self.t0 = self.t1 = None
 
     def start(self):
         out = ROOT / "gpurun_out"
@@ -103,28 +106,52 @@ class ClockSampler:
         except OSError:
             self.proc = None
 
+    def wait_ready(self, timeout=10.0):
+        """Block until the first sample is on disk (nvidia-smi takes a moment
+        to start on a many-GPU box), so the timed window is covered."""
+        deadline = time.time() + timeout
+        while self.proc is not None and time.time() < deadline:
+            if self.path.exists() and self.path.stat().st_size > 0:
+                return
+            time.sleep(0.05)
+
+    def window(self, t0, t1):
+        self.t0, self.t1 = t0, t1
+
     def stop(self):
         if self.proc is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        if self.t1 is not None:  # a few samples past the window's end
+            time.sleep(max(0.0, self.t1 + 0.15 - time.time()))
         self.proc.terminate()
         self.proc.wait(timeout=10)
-        sm, mx, reasons = [], [], set()
+        import datetime
+
+        rows = []
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for line in self.path.read_text().splitlines():
             parts = [x.strip() for x in line.split(",")]
-            if len(parts) < 9:
+            if len(parts) < 10:
                 continue
+            when = None
+            for fmt in ("%Y/%m/%d %H:%M:%S.%f", "%Y/%m/%d %H:%M:%S"):
+                try:
+                    when = datetime.datetime.strptime(parts[0], fmt).timestamp()
+                    break
+                except ValueError:
+                    pass
             try:
-                sm.append(float(parts[1]))
-                mx.append(float(parts[2]))
+                rows.append((when, float(parts[2]), float(parts[3]),
+                             {n for n, f in zip(names, parts[6:10]) if f.lower().startswith("active")}))
             except ValueError:
                 continue
-            for name, flag in zip(names, parts[5:9]):
-                if flag.lower().startswith("active"):
-                    reasons.add(name)
-        return {"sm_mhz": float(np.median(sm)) if sm else None,
-                "sm_max_mhz": max(mx) if mx else None, "reasons": sorted(reasons),
-                "samples": len(sm)}
+        inside = [r for r in rows if self.t0 is not None and r[0] is not None
+                  and self.t0 - 0.05 <= r[0] <= self.t1 + 0.05]
+        chosen, where = (inside, "timed region") if len(inside) >= 2 else (rows, "whole run")
+        reasons = set().union(*[r[3] for r in chosen]) if chosen else set()
+        return {"sm_mhz": float(np.median([r[1] for r in chosen])) if chosen else None,
+                "sm_max_mhz": max(r[2] for r in chosen) if chosen else None,
+                "reasons": sorted(reasons), "samples": len(chosen), "window": where}
 
 
 # ---------------------------------------------------------------------------
@@ -330,18 +357,21 @@ def run_gpu(args, rank, world, local_rank, log):
     # decode steady state: the hot buffers fill up (4096 rows a unit, ~440 misses
     # a step) before the W warm-up steps, as they are after the first dozen tokens
     settle = torch.zeros((SETTLE_STEPS, LAYERS, REQUESTS, 3), dtype=torch.int64, device=device)
-    run_steps(0, SETTLE_STEPS, graph, settle_base, settle)
-    run_steps(0, warmup)
-    barrier()
-    # ---- timed region: K steps, device-resident inputs ------------------------------
     sampler = ClockSampler(local_rank)
     sampler.start()
+    run_steps(0, SETTLE_STEPS, graph, settle_base, settle)
+    run_steps(0, warmup)
+    sampler.wait_ready()
+    barrier()
+    # ---- timed region: K steps, device-resident inputs ------------------------------
     start = torch.cuda.Event(enable_timing=True)
     end = torch.cuda.Event(enable_timing=True)
+    wall0 = time.time()
     start.record(compute)
     run_steps(warmup, total)
     end.record(compute)
     barrier()
+    sampler.window(wall0, time.time())
     clocks = sampler.stop()
     elapsed_ms = max_over_ranks(start.elapsed_time(end))
     timed_counts = counts[warmup:].cpu().numpy()  # [steps, L, B, 3]

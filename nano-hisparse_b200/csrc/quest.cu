@@ -464,6 +464,9 @@ __global__ void __launch_bounds__(kTmaThreads, 1) quest_tma_kernel(QuestParams<T
     const int d0 = lane * C;
     constexpr bool kFma = is16<TQ>() && is16<TKV>();
     int cur = -1;
+    // 16-bit data: q+ and q- held as duplicated pairs, the packed FMA's first
+    // operand for two pages at once (hoisted: a warp keeps its item's heads)
+    float2 qa2[kHeadsPerItem][C], qb2[kHeadsPerItem][C];
     float qa[kHeadsPerItem][C], qb[kHeadsPerItem][C];
     for (int g = 0; g < nstages; ++g) {
       const int64_t pages = min((int64_t)kTmaStagePages, tile_n - (int64_t)g * kTmaStagePages);
@@ -486,41 +489,53 @@ __global__ void __launch_bounds__(kTmaThreads, 1) quest_tma_kernel(QuestParams<T
 #pragma unroll
             for (int c = 0; c < C; ++c) {
               const float v = hh < h_count ? to_f32(q[(int64_t)(h_begin + hh) * D + d0 + c]) : 0.f;
-              qa[hh][c] = kFma ? fmaxf(v, 0.f) : v;
-              qb[hh][c] = kFma ? fminf(v, 0.f) : v;
+              if constexpr (kFma) {
+                qa2[hh][c] = make_float2(fmaxf(v, 0.f), fmaxf(v, 0.f));
+                qb2[hh][c] = make_float2(fminf(v, 0.f), fminf(v, 0.f));
+              } else {
+                qa[hh][c] = v;
+                qb[hh][c] = v;
+              }
             }
         }
         float v[32];
 #pragma unroll
         for (int i = 0; i < kPagesPerItem; i += 2) {
-          // pages i and i+1 side by side: one packed fp32x2 FMA serves both
-          float l0[C], h0[C], l1[C], h1[C];
-          {
-            const int lp = pgi * kPagesPerItem + i;
-            Raw<TKV, C> rl0, rh0, rl1, rh1;
-            rl0.load_shared_full(lo_s + lp * (int)page_elems + kh * D + d0, lp < pages);
-            rh0.load_shared_full(hi_s + lp * (int)page_elems + kh * D + d0, lp < pages);
-            rl1.load_shared_full(lo_s + (lp + 1) * (int)page_elems + kh * D + d0, lp + 1 < pages);
-            rh1.load_shared_full(hi_s + (lp + 1) * (int)page_elems + kh * D + d0, lp + 1 < pages);
+          // pages i and i+1 side by side: one packed fp32x2 FMA serves both.
+          // Rows past the tile's last page hold stale data; their sums are
+          // never stored (lp < pages below), so the loads need no predicate.
+          const int lp = pgi * kPagesPerItem + i;
+          Raw<TKV, C> rl0, rh0, rl1, rh1;
+          rl0.load_shared_full(lo_s + lp * (int)page_elems + kh * D + d0, true);
+          rh0.load_shared_full(hi_s + lp * (int)page_elems + kh * D + d0, true);
+          rl1.load_shared_full(lo_s + (lp + 1) * (int)page_elems + kh * D + d0, true);
+          rh1.load_shared_full(hi_s + (lp + 1) * (int)page_elems + kh * D + d0, true);
+          if constexpr (kFma) {
+            float2 part[kHeadsPerItem];
+#pragma unroll
+            for (int c = 0; c < C; ++c) {
+              // the two pages' element c, widened straight into a packed pair
+              const float2 hi2 = make_float2(to_f32(rh0.e[c]), to_f32(rh1.e[c]));
+              const float2 lo2 = make_float2(to_f32(rl0.e[c]), to_f32(rl1.e[c]));
+#pragma unroll
+              for (int hh = 0; hh < kHeadsPerItem; ++hh) {
+                part[hh] = __ffma2_rn(qa2[hh][c], hi2, c == 0 ? make_float2(0.f, 0.f) : part[hh]);
+                part[hh] = __ffma2_rn(qb2[hh][c], lo2, part[hh]);
+              }
+            }
+#pragma unroll
+            for (int hh = 0; hh < kHeadsPerItem; ++hh) {
+              v[i * kHeadsPerItem + hh] = part[hh].x;
+              v[(i + 1) * kHeadsPerItem + hh] = part[hh].y;
+            }
+          } else {
+            float l0[C], h0[C], l1[C], h1[C];
             rl0.unpack(l0);
             rh0.unpack(h0);
             rl1.unpack(l1);
             rh1.unpack(h1);
-          }
 #pragma unroll
-          for (int hh = 0; hh < kHeadsPerItem; ++hh) {
-            if constexpr (kFma) {
-              float2 part = make_float2(0.f, 0.f);
-#pragma unroll
-              for (int c = 0; c < C; ++c) {
-                part = __ffma2_rn(make_float2(qa[hh][c], qa[hh][c]), make_float2(h0[c], h1[c]),
-                                  c == 0 ? make_float2(0.f, 0.f) : part);
-                part = __ffma2_rn(make_float2(qb[hh][c], qb[hh][c]), make_float2(l0[c], l1[c]),
-                                  part);
-              }
-              v[i * kHeadsPerItem + hh] = part.x;
-              v[(i + 1) * kHeadsPerItem + hh] = part.y;
-            } else {
+            for (int hh = 0; hh < kHeadsPerItem; ++hh) {
               float p0 = 0.f, p1 = 0.f;
 #pragma unroll
               for (int c = 0; c < C; ++c) {
