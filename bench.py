@@ -570,6 +570,172 @@ def run_gpu(args, rank, world, local_rank, log):
 
 
 # ---------------------------------------------------------------------------
+# configuration 5: one 1M-token request, KV heads split over the ranks
+# ---------------------------------------------------------------------------
+C5 = {"layers": 28, "q_heads": 28, "kv_heads": 4, "head_dim": 128, "page_size": 64,
+      "context": 1 << 20, "top_pages": 128, "resident_fraction": 0.10, "hot_rows": 16384}
+
+
+def run_config5(args, rank, world, local_rank, log):
+    """Decode of one 1,048,576-token request of a Qwen2.5-7B-shaped model (28
+    layers, 28 query / 4 KV heads, page 64, 10 % resident) with its KV heads
+    split over `world` ranks: per layer, each rank's partial Quest scores
+    are all-gathered (NCCL) and every rank takes the same top-128 pages, then
+    resolves, gathers and attends over its own head slice. Strong scaling:
+    the request is the same at every N."""
+    import torch.distributed as dist
+
+    from hisparse_b200 import CacheConfig, DecodeBatch, HotConfig, RowCache
+    from hisparse_b200.sharding import bind_to_device_node
+
+    c = C5
+    if c["kv_heads"] % world:
+        raise SystemExit(f"configuration 5 splits {c['kv_heads']} KV heads: use 1, 2 or 4 GPUs")
+    hkv, hq = c["kv_heads"] // world, c["q_heads"] // world
+    L, P, D = c["layers"], c["page_size"], c["head_dim"]
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    bind_to_device_node(local_rank)
+    hbm_peak, _ = measured_peaks()
+    link_peak = hostlink_peak(device)
+    n = c["context"] // P
+    hot = HotConfig(c["top_pages"] * P, c["hot_rows"])
+    hot_blocks = hot.hot_blocks(P)
+    resident_pages = int(round(n * c["resident_fraction"]))
+    page_bytes = 2 * P * hkv * D * 2
+    host_pages = host_store_pages(L * n, page_bytes, log)
+    config = CacheConfig(gpu_pages=L * (resident_pages + hot_blocks), host_pages=host_pages,
+                         page_size=P, kv_heads=hkv, head_dim=D, device=str(device), dtype=DTYPE,
+                         index_budget_bytes=1 << 40)
+    host = torch.empty((host_pages, 2, P, hkv, D), dtype=DTYPE, pin_memory=True)
+    cache = RowCache(config, hot, host=host)
+    gen = torch.Generator(device=device).manual_seed(1 + rank)  # this rank's head slice
+    rng = np.random.default_rng(5)  # placement: the same on every rank (replicated tables)
+    mins = torch.empty((L, n, hkv, D), dtype=DTYPE, device=device)
+    maxs = torch.empty_like(mins)
+    block = 0
+    for layer in range(L):
+        base = (layer * n) % (host_pages - n + 1)
+        for lo in range(0, n, 4096):
+            kv = torch.randn((min(4096, n - lo), 2, P, hkv, D), generator=gen, device=device,
+                             dtype=torch.float32).to(DTYPE)
+            mins[layer, lo:lo + len(kv)] = kv[:, 0].amin(1)
+            maxs[layer, lo:lo + len(kv)] = kv[:, 0].amax(1)
+            host[base + lo:base + lo + len(kv)].copy_(kv, non_blocking=True)
+        torch.cuda.synchronize(device)  # the host rows are read back below
+        chosen = rng.choice(n - 2, size=resident_pages - 2, replace=False)
+        pages = np.sort(np.concatenate([chosen, [n - 2, n - 1]]))
+        resident = np.full(n, -1, dtype=np.int64)
+        resident[pages] = np.arange(block, block + resident_pages)
+        cache.pool[block:block + resident_pages] = host[torch.from_numpy(base + pages)].to(device)
+        block += resident_pages
+        hot_list = list(range(block, block + hot_blocks))
+        block += hot_blocks
+        cache.add_layer(0, layer, c["context"], np.arange(base, base + n), resident, hot_list)
+    torch.cuda.synchronize(device)
+    group = dist.group.WORLD if world > 1 else None
+    streams = (torch.cuda.Stream(device=device), torch.cuda.Stream(device=device))
+    batch = DecodeBatch(cache, [0], L, {0: mins}, {0: maxs}, c["top_pages"], hq, group=group,
+                        streams=streams)
+    steps, warmup, settle = args.steps, args.warmup, 2
+    total = settle + warmup + steps
+    qgen = torch.Generator(device=device).manual_seed(1000 + rank)
+    queries = torch.randn((total, L, 1, hq, D), generator=qgen, device=device,
+                          dtype=torch.float32).to(DTYPE)
+    counts = torch.zeros((total, L, 1, 3), dtype=torch.int64, device=device)
+    out = torch.empty((1, hq, D), dtype=DTYPE, device=device)
+
+    def run(first, last):
+        with torch.cuda.stream(batch.compute):
+            for s_ in range(first, last):
+                for layer in range(L):
+                    batch.layer(layer, queries[s_, layer], out, counts[s_, layer])
+
+    def barrier():
+        torch.cuda.synchronize(device)
+        if world > 1:
+            dist.barrier()
+
+    run(0, settle + warmup)
+    barrier()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(batch.compute)
+    run(settle + warmup, total)
+    end.record(batch.compute)
+    barrier()
+    ms = start.elapsed_time(end)
+    if world > 1:
+        t = torch.tensor([ms], dtype=torch.float64, device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    timed = counts[settle + warmup:].cpu().numpy()
+    graph_ms = None
+    if world == 1:  # the same steps replayed from one captured graph (no collective to capture)
+        from hisparse_b200.batched import DecodeGraph
+
+        graph = DecodeGraph([batch], L)
+        gq = torch.randn((warmup + steps, L, 1, hq, D), generator=qgen, device=device,
+                         dtype=torch.float32).to(DTYPE)
+        for s_ in range(warmup):
+            graph.queries[0].copy_(gq[s_])
+            graph.replay()
+        torch.cuda.synchronize(device)
+        g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        g0.record()
+        for s_ in range(warmup, warmup + steps):
+            graph.queries[0].copy_(gq[s_])
+            graph.replay()
+        g1.record()
+        torch.cuda.synchronize(device)
+        graph_ms = g0.elapsed_time(g1)
+        for st in batch.layers:
+            st.ready = st.last_use = None
+        del graph
+    # per-stage device time: one more step, each stage alone (CUDA events on its stream)
+    timing = []
+    extra = torch.randn((L, 1, hq, D), generator=qgen, device=device,
+                        dtype=torch.float32).to(DTYPE)
+    with torch.cuda.stream(batch.compute):
+        for layer in range(L):
+            torch.cuda._sleep(1_000_000)
+            batch.layer(layer, extra[layer], out, None, timing, serial=True)
+    barrier()
+    stage_ms = {}
+    for name, a_, b_ in timing:
+        stage_ms[name] = stage_ms.get(name, 0.0) + a_.elapsed_time(b_)
+    row_bytes = 2 * hkv * D * 2
+    misses = int(timed[..., 2].sum())
+    hostlink_bytes = misses * row_bytes / steps
+    selected = int(timed.sum()) / steps
+    hbm_bytes = L * 2 * n * hkv * D * 2 + selected * row_bytes + hostlink_bytes
+    t_roof = max(hbm_bytes / (hbm_peak * 1e9), hostlink_bytes / (link_peak * 1e9))
+    flags = __import__("hisparse_b200")._lib.device_flags(device)
+    if flags:
+        raise RuntimeError(f"device flags raised: {flags}")
+    return {
+        "metric": "decode tok/s, one 1M-token request, KV heads split over the GPUs",
+        "value": round(steps / (ms * 1e-3), 2), "unit": "tok/s", "n_gpus": world, "steps": steps,
+        "warmup": warmup, "ms_per_step": round(ms / steps, 3), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": "config 5: Qwen2.5-7B-shaped decode of one 1M-token request, "
+                               "KV heads sharded, per-layer all-gather of partial Quest scores",
+                   **c, "kv_heads_per_rank": hkv, "q_heads_per_rank": hq,
+                   "host_store_gib_per_rank": round(host_pages * page_bytes / 2**30, 2)},
+        "exchange_bytes_per_layer": 4 * n * world,
+        "stage_ms_per_step": {k: round(v, 3) for k, v in stage_ms.items()},
+        "graph_tok_s": None if graph_ms is None else round(steps / (graph_ms * 1e-3), 2),
+        "stage_note": "one extra step, every stage timed alone; quest includes the all-gather",
+        "per_rank": {"miss_rows_per_layer": round(misses / (steps * L), 1),
+                     "hostlink_bytes_per_step": int(hostlink_bytes),
+                     "hbm_bytes_per_step": int(hbm_bytes),
+                     "gather_gbs_avg": round(hostlink_bytes / (ms / steps * 1e-3) / 1e9, 2),
+                     "hostlink_peak_gbs": round(link_peak, 2),
+                     "t_roof_ms": round(t_roof * 1e3, 3),
+                     "step_roofline_frac": round(t_roof / (ms / steps * 1e-3), 4)},
+    }
+
+
+# ---------------------------------------------------------------------------
 # CPU arm (oracle restatement of the reference's path)
 # ---------------------------------------------------------------------------
 def cpu_sample(seed=1, budget_s=10.0, threads=None, log=print):
@@ -655,6 +821,9 @@ def main():
     parser.add_argument("--transfer", choices=["shared", "separate"], default=TRANSFER,
                         help="one transfer stream for all micro-batches (gathers take the "
                              "host link in turn) or one each")
+    parser.add_argument("--workload", choices=["config2", "config5"], default="config2",
+                        help="config2 (the bench line) or config5 (one 1M-token request, KV "
+                             "heads split over 1, 2 or 4 GPUs)")
     parser.add_argument("--requests", type=int, default=REQUESTS)
     parser.add_argument("--layers", type=int, default=LAYERS)
     args = parser.parse_args()
@@ -695,6 +864,11 @@ def main():
                                 device_id=torch.device("cuda", local_rank))
     try:
         all_cpus = os.sched_getaffinity(0)
+        if args.workload == "config5":
+            result = run_config5(args, rank, world, local_rank, log)
+            if rank == 0:
+                print(json.dumps(result), flush=True)
+            return
         result = run_gpu(args, rank, world, local_rank, log)
         os.sched_setaffinity(0, all_cpus)  # the CPU baseline uses every host core
         if rank == 0:

@@ -162,7 +162,21 @@ __device__ void select_request(const QuestParams<TQ, TKV> &p, int b, int64_t len
   const bool sink = p.keep_sink && p.top_pages > 1 && n > 1;
   KeySource key_of{nullptr, sc, n, sink};
   if (key_cache != nullptr && n <= kSmemKeys) {
-    for (int64_t pg = tid; pg < n; pg += blockDim.x) key_cache[pg] = page_key(sc, pg, n, sink);
+    // eight independent score loads in flight per thread (the scores sit in L2:
+    // one load at a time would cost a full L2 round trip per page)
+    for (int64_t pg0 = tid; pg0 < n; pg0 += 8 * (int64_t)blockDim.x) {
+      uint32_t key[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int64_t pg = pg0 + (int64_t)u * blockDim.x;
+        key[u] = pg < n ? page_key(sc, pg, n, sink) : 0u;
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int64_t pg = pg0 + (int64_t)u * blockDim.x;
+        if (pg < n) key_cache[pg] = key[u];
+      }
+    }
     key_of.cached = key_cache;
   }
   if (tid == 0) {
@@ -610,11 +624,25 @@ __global__ void __launch_bounds__(kSelectThreads)
   const int64_t n = length > 0 ? ceil_div(length, (int64_t)p.page_size) : 0;
   float *sc = p.scores + (int64_t)b * p.max_pages;
   if (n <= p.max_pages) {
-    for (int64_t pg = threadIdx.x; pg < n; pg += blockDim.x) {
-      float total = 0.f;
-      for (int r = 0; r < shards; ++r)
-        total = __fadd_rn(total, partials[((int64_t)r * p.batch + b) * p.max_pages + pg]);
-      sc[pg] = __fdiv_rn(total, (float)p.q_heads);
+    // four pages per thread at a time, their shard loads all in flight
+    for (int64_t pg0 = threadIdx.x; pg0 < n; pg0 += 4 * (int64_t)blockDim.x) {
+      float total[4] = {0.f, 0.f, 0.f, 0.f};
+      for (int r = 0; r < shards; ++r) {
+        const float *row = partials + ((int64_t)r * p.batch + b) * p.max_pages;
+        float v[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int64_t pg = pg0 + (int64_t)u * blockDim.x;
+          v[u] = pg < n ? __ldcg(row + pg) : 0.f;
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) total[u] = __fadd_rn(total[u], v[u]);
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int64_t pg = pg0 + (int64_t)u * blockDim.x;
+        if (pg < n) sc[pg] = __fdiv_rn(total[u], (float)p.q_heads);
+      }
     }
   }
   __syncthreads();

@@ -55,12 +55,19 @@ class DecodeBatch:
     """
 
     def __init__(self, cache: RowCache, request_ids, layers, minimum, maximum, top_pages,
-                 q_heads, keep_sink=True, streams=None):
+                 q_heads, keep_sink=True, streams=None, group=None):
         """streams: optional (compute, transfer) CUDA streams for this batch; by
         default the cache's. Batches over disjoint requests with their own
         compute streams run concurrently (micro-batch pipelining: one batch's
         gather overlaps another's selection, resolve and attention); sharing one
-        transfer stream makes their gathers take the host link in turn."""
+        transfer stream makes their gathers take the host link in turn.
+
+        group: a process group over which the requests' KV heads are split
+        (configuration 5). This rank then holds kv_heads of the cache config
+        and q_heads of the queries; the page selection becomes the
+        head-sharded one (partial scores, an all-gather over `group`, the
+        shared top-k), identical on every rank, and resolve, gather and
+        attention run over this rank's head slice."""
         self.cache, self.request_ids = cache, list(request_ids)
         if streams is None:
             self.compute, self.transfer = cache.compute, cache.transfer
@@ -91,6 +98,14 @@ class DecodeBatch:
         self.attend_ws_bytes = lib.hs_attend_workspace_bytes(b, q_heads, cfg.kv_heads,
                                                              cfg.head_dim, self.width)
         self.attend_ws = _lib.workspace(self.attend_ws_bytes, dev)
+        self.group, self.shards = group, 1
+        if group is not None:
+            import torch.distributed as dist
+
+            self.shards = dist.get_world_size(group)
+            self.partial = torch.empty(b * self.max_pages, dtype=torch.float32, device=dev)
+            self.partials = torch.empty((self.shards, b * self.max_pages), dtype=torch.float32,
+                                        device=dev)
         self.status = _lib.status_word(dev)
         self._dtype = _lib.dtype_code(cfg.dtype)
         self._row_bytes = cfg.row_bytes
@@ -140,12 +155,27 @@ class DecodeBatch:
         if st.ready is not None:
             compute.wait_event(st.ready)
         t0 = mark(compute, "quest")
-        _lib.check(lib.hs_quest_select_batched(
-            b, query.data_ptr(), hq * d, _lib.dtype_code(query.dtype), st.min_ptrs.data_ptr(),
-            st.max_ptrs.data_ptr(), self._dtype, st.lengths.data_ptr(), hq, cfg.kv_heads, d,
-            self.max_pages, cfg.page_size, self.top_pages, int(self.keep_sink),
-            self.tokens.data_ptr(), self.width, self.token_counts.data_ptr(),
-            _lib.ptr(self.quest_ws), self.quest_ws_bytes, status, stream))
+        if self.group is None:
+            _lib.check(lib.hs_quest_select_batched(
+                b, query.data_ptr(), hq * d, _lib.dtype_code(query.dtype), st.min_ptrs.data_ptr(),
+                st.max_ptrs.data_ptr(), self._dtype, st.lengths.data_ptr(), hq, cfg.kv_heads, d,
+                self.max_pages, cfg.page_size, self.top_pages, int(self.keep_sink),
+                self.tokens.data_ptr(), self.width, self.token_counts.data_ptr(),
+                _lib.ptr(self.quest_ws), self.quest_ws_bytes, status, stream))
+        else:
+            import torch.distributed as dist
+
+            # this rank's head sums, every rank's in shard order, the shared top-k
+            _lib.check(lib.hs_quest_partial_scores_batched(
+                b, query.data_ptr(), hq * d, _lib.dtype_code(query.dtype), st.min_ptrs.data_ptr(),
+                st.max_ptrs.data_ptr(), self._dtype, st.lengths.data_ptr(), hq, cfg.kv_heads, d,
+                self.max_pages, cfg.page_size, self.partial.data_ptr(), status, stream))
+            dist.all_gather_into_tensor(self.partials, self.partial, group=self.group)
+            _lib.check(lib.hs_quest_select_partials(
+                self.shards, self.partials.data_ptr(), b, st.lengths.data_ptr(), hq * self.shards,
+                self.max_pages, cfg.page_size, self.top_pages, int(self.keep_sink),
+                self.tokens.data_ptr(), self.width, self.token_counts.data_ptr(),
+                _lib.ptr(self.quest_ws), self.quest_ws_bytes, status, stream))
         t1 = mark(compute, "quest", "resolve")
         _lib.check(lib.hs_resolve_rows_batched(
             b, self.tokens.data_ptr(), self.width, st.src_ptrs.data_ptr(), st.res_ptrs.data_ptr(),
@@ -229,6 +259,10 @@ class DecodeGraph:
         after a replay ``self.timing`` holds that replay's (name, start, end)
         pairs for every (layer, batch)."""
         self.batches, self.layers = list(batches), layers
+        for bt in self.batches:
+            if bt.compute.cuda_stream == 0 or bt.transfer.cuda_stream == 0:
+                raise ValueError("DecodeGraph needs batches on created streams, not the default "
+                                 "stream (pass streams=(compute, transfer) to DecodeBatch)")
         b0 = self.batches[0]
         self.device = b0.device
         dt = b0.config.dtype

@@ -167,3 +167,77 @@ def test_two_ranks_over_nccl_agree_with_emulation():
                        start_method="spawn", join=True)
     for rank in range(2):
         assert [t for t in out[rank] if t >= 0] == expected
+
+
+def _batch_rank(rank, world, port, q, keys, length, p, top, out):
+    """One rank of a head-sharded DecodeBatch layer over its KV-head slice."""
+    import sys
+    from pathlib import Path
+
+    import numpy as np
+
+    root = Path(__file__).resolve().parent.parent
+    sys.path.insert(0, str(root / "nano-hisparse_b200"))
+    import datetime
+
+    import torch.distributed as dist
+
+    from hisparse_b200 import CacheConfig, DecodeBatch, HotConfig, RowCache
+    from hisparse_b200 import _lib as lib_
+    from hisparse_b200.sharded import head_slice as hs_slice
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60), device_id=dev)
+    try:
+        ks, qs = hs_slice(keys.shape[3], q.shape[0], rank, world)
+        kv = keys[:, :, :, ks].contiguous()                  # [n, 2, P, Hkv_l, D]
+        n, hkv, d = kv.shape[0], kv.shape[3], kv.shape[4]
+        hot = HotConfig(top * p, 2 * top * p)
+        hb = hot.hot_blocks(p)
+        resident = np.full(n, -1)
+        resident[[0, n - 2, n - 1]] = [0, 1, 2]
+        config = CacheConfig(gpu_pages=3 + hb, host_pages=n, page_size=p, kv_heads=hkv,
+                             head_dim=d, device=str(dev), dtype=kv.dtype)
+        cache = RowCache(config, hot, host=kv.pin_memory())
+        cache.pool.zero_()
+        cache.pool[:3] = kv[[0, n - 2, n - 1]].to(dev)
+        cache.add_layer(0, 0, length, np.arange(n), resident, list(range(3, 3 + hb)))
+        mins = kv[:, 0].float().amin(1).to(kv.dtype)[None].to(dev)
+        maxs = kv[:, 0].float().amax(1).to(kv.dtype)[None].to(dev)
+        batch = DecodeBatch(cache, [0], 1, {0: mins}, {0: maxs}, top, q[qs].shape[0],
+                            group=dist.group.WORLD)
+        counts = torch.zeros((1, 3), dtype=torch.int64, device=dev)
+        with torch.cuda.stream(batch.compute):
+            o = batch.layer(0, q[qs][None].to(dev).contiguous(), counts=counts)
+        torch.cuda.synchronize(dev)
+        out[rank] = (batch.tokens[0].cpu().tolist(), counts.cpu().tolist(),
+                     bool(torch.isfinite(o).all()), lib_.device_flags(dev))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_head_sharded_decode_batch_on_two_ranks():
+    """DecodeBatch with a process group: both ranks select the same pages (the
+    emulated sharded selection of the whole request), make the same plan and
+    attend over their own heads."""
+    import torch.multiprocessing as mp
+
+    gen = torch.Generator().manual_seed(12)
+    hq, hkv, d, p, length, top = 8, 4, 64, 16, 3000, 12
+    n = math.ceil(length / p)
+    q = torch.randn(hq, d, generator=gen).to(torch.bfloat16)
+    keys = torch.randn(n, 2, p, hkv, d, generator=gen).to(torch.bfloat16)
+    mn = keys[:, 0].float().amin(1).to(torch.bfloat16)
+    mx = keys[:, 0].float().amax(1).to(torch.bfloat16)
+    expected, _ = _emulated(q.to(DEV), mn.to(DEV), mx.to(DEV), length, p, top, True, 2)
+    manager = mp.get_context("spawn").Manager()
+    out = manager.dict()
+    mp.start_processes(_batch_rank, args=(2, _free_port(), q, keys, length, p, top, out),
+                       nprocs=2, start_method="spawn", join=True)
+    assert [t for t in out[0][0] if t >= 0] == expected
+    assert out[0][0] == out[1][0] and out[0][1] == out[1][1]
+    assert out[0][2] and out[1][2] and not out[0][3] and not out[1][3]
