@@ -81,3 +81,48 @@ def test_operators_refuse_cpu_tensors():
     t = torch.zeros(4, dtype=torch.int32)
     with pytest.raises(ValueError, match="CUDA"):
         resolve_rows(LogicalTopK(t), t, t, t, t, t.long(), 16, 4)
+
+
+def test_host_side_validation_of_append_and_sharded_selection():
+    """Argument errors of the append and head-sharded selection entry points
+    are reported on the host, before any device work."""
+    lib = _lib.load()
+    d = 256  # a dummy non-null pointer value: never dereferenced on these paths
+    # append: negative batch, bad head shape, unknown dtype, null pointers
+    assert lib.hs_append_rows(-1, d, d, 0, _lib.HS_BFLOAT16, d, d, d, d, 1, d, d, 1, d, d, d,
+                              8, 128, 16, None, None) == _lib.HS_ERR_INVALID_ARGUMENT
+    assert lib.hs_append_rows(1, d, d, 0, _lib.HS_BFLOAT16, d, d, d, d, 1, d, d, 1, d, d, d,
+                              0, 128, 16, None, None) == _lib.HS_ERR_INVALID_ARGUMENT
+    assert lib.hs_append_rows(1, None, d, 0, _lib.HS_BFLOAT16, d, d, d, d, 1, d, d, 1, d, d, d,
+                              8, 128, 16, None, None) == _lib.HS_ERR_INVALID_ARGUMENT
+    assert b"null" in lib.hs_last_error()
+    assert lib.hs_append_rows(0, None, None, 0, _lib.HS_BFLOAT16, None, None, None, None, 0,
+                              None, None, 0, None, None, None, 8, 128, 16, None,
+                              None) == _lib.HS_OK  # an empty batch is a no-op
+    # sharded selection: no shards, a too small output, a missing workspace
+    assert lib.hs_quest_select_partials(0, d, 1, d, 28, 16384, 64, 128, 1, d, 8192, d, d,
+                                        1 << 20, None, None) == _lib.HS_ERR_INVALID_ARGUMENT
+    assert lib.hs_quest_select_partials(2, d, 1, d, 28, 16384, 64, 128, 1, d, 100, d, d,
+                                        1 << 20, None, None) == _lib.HS_ERR_INVALID_ARGUMENT
+    assert b"out_capacity" in lib.hs_last_error()
+    assert lib.hs_quest_select_partials(2, d, 1, d, 28, 16384, 64, 128, 1, d, 8192, d, None, 0,
+                                        None, None) == _lib.HS_ERR_WORKSPACE
+    assert lib.hs_quest_partial_scores_batched(1, d, 0, _lib.HS_BFLOAT16, d, d, _lib.HS_BFLOAT16,
+                                               d, 14, 2, 128, 16384, 64, None, None,
+                                               None) == _lib.HS_ERR_INVALID_ARGUMENT
+    assert lib.hs_quest_partial_scores_batched(1, d, 0, _lib.HS_BFLOAT16, d, d, _lib.HS_BFLOAT16,
+                                               d, 14, 4, 128, 16384, 64, d, None,
+                                               None) == _lib.HS_ERR_INVALID_ARGUMENT
+    assert lib.hs_last_error() == b"invalid page budget or GQA shape"
+
+
+def test_sharded_head_slices():
+    from hisparse_b200.sharded import head_slice
+
+    assert head_slice(4, 28, 1, 2) == (slice(2, 4), slice(14, 28))
+    assert [head_slice(8, 32, r, 4)[0] for r in range(4)] == [slice(0, 2), slice(2, 4),
+                                                              slice(4, 6), slice(6, 8)]
+    with pytest.raises(ValueError):
+        head_slice(4, 28, 0, 3)
+    with pytest.raises(ValueError):
+        head_slice(4, 28, 2, 2)
