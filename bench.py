@@ -95,8 +95,11 @@ class ClockSampler:
         self.t0 = self.t1 = None
 
     def start(self):
-        out = ROOT / "gpurun_out"
-        out.mkdir(exist_ok=True)
+        import tempfile
+
+        # raw samples: HS_BENCH_LOG_DIR when set (to keep them), else a temp dir
+        out = Path(os.environ.get("HS_BENCH_LOG_DIR", tempfile.gettempdir()))
+        out.mkdir(parents=True, exist_ok=True)
         self.path = out / f"clocks_rank{self.index}.csv"
         try:
             self.proc = subprocess.Popen(
