@@ -125,6 +125,7 @@ __device__ __forceinline__ uint32_t page_key(const float *sc, int64_t page, int6
 }
 
 constexpr int kSmemKeys = 16384;  // pages whose keys the select phase caches in shared memory
+constexpr int kMaxChosenPages = 2048;  // chosen-page list of the cooperative token expansion
 
 // Keys of one request: from shared memory when cached, else recomputed from
 // the scores in global memory.
@@ -219,34 +220,87 @@ __device__ void select_request(const QuestParams<TQ, TKV> &p, int b, int64_t len
   }
   const uint32_t threshold = s_prefix;
   const int64_t take_equal = s_k;  // keys == threshold to keep, lowest pages first
-  const int64_t per = ceil_div(n, (int64_t)blockDim.x);
-  const int64_t lo = min(n, tid * per), hi = min(n, lo + per);
+  // Keep every key above the threshold and the first take_equal keys equal to
+  // it, in page order. Warp-major: warp w owns the pages [w*span, (w+1)*span)
+  // (span a multiple of 32) and walks them 32 at a time with lane = page, so
+  // the shared-memory key reads are consecutive; ballots give each lane the
+  // number of equal and of chosen pages before it.
+  const int lane = tid & 31, warp = tid >> 5, warps = (int)(blockDim.x >> 5);
+  const unsigned before_me = (1u << lane) - 1u;
+  const int64_t span = ceil_div(ceil_div(n, (int64_t)warps), 32) * 32;
+  const int64_t w_lo = min(n, warp * span), w_hi = min(n, w_lo + span);
   int64_t eq_local = 0;
-  for (int64_t pg = lo; pg < hi; ++pg) eq_local += key_of(pg) == threshold;
+  for (int64_t base = w_lo; base < w_hi; base += 32) {
+    const int64_t pg = base + lane;
+    eq_local += __popc(__ballot_sync(kFullMask, pg < w_hi && key_of(pg) == threshold));
+  }
   int64_t eq_total;
-  const int64_t eq_before = block_exclusive_scan<int64_t>(eq_local, scan_scratch, &eq_total);
+  // lane 0 carries its warp's count; the other lanes take lane 0's prefix
+  const int64_t eq_before = __shfl_sync(
+      kFullMask, block_exclusive_scan<int64_t>(lane == 0 ? eq_local : 0, scan_scratch, &eq_total),
+      0);
+  // one step of the walk: is this lane's page chosen? (eq_run: equal keys before the step)
+#define HS_TAKE(pg, eq_run, eq_mask)                                                     \
+  ([&]() -> bool {                                                                       \
+    const uint32_t key_ = (pg) < w_hi ? key_of(pg) : 0u;                                 \
+    const bool eq_ = (pg) < w_hi && key_ == threshold;                                   \
+    eq_mask = __ballot_sync(kFullMask, eq_);                                             \
+    return ((pg) < w_hi && key_ > threshold) ||                                          \
+           (eq_ && (eq_run) + __popc(eq_mask & before_me) < take_equal);                 \
+  }())
   int64_t chosen_local = 0;
   {
-    int64_t eq = eq_before;
-    for (int64_t pg = lo; pg < hi; ++pg) {
-      const uint32_t key = key_of(pg);
-      chosen_local += key > threshold || (key == threshold && eq++ < take_equal);
+    int64_t eq_run = eq_before;
+    for (int64_t base = w_lo; base < w_hi; base += 32) {
+      unsigned eq_mask;
+      const bool t = HS_TAKE(base + lane, eq_run, eq_mask);
+      chosen_local += __popc(__ballot_sync(kFullMask, t));
+      eq_run += __popc(eq_mask);
     }
   }
   int64_t chosen_total;
-  int64_t rank = block_exclusive_scan<int64_t>(chosen_local, scan_scratch, &chosen_total);
-  {
-    int64_t eq = eq_before;
-    for (int64_t pg = lo; pg < hi; ++pg) {
-      const uint32_t key = key_of(pg);
-      if (key > threshold || (key == threshold && eq++ < take_equal)) {
+  const int64_t chosen_before = __shfl_sync(
+      kFullMask,
+      block_exclusive_scan<int64_t>(lane == 0 ? chosen_local : 0, scan_scratch, &chosen_total),
+      0);
+  if (chosen_total <= kMaxChosenPages) {
+    // the chosen pages by rank, then every thread writes tokens: coalesced
+    // stores spread over the block instead of a page's tokens from one thread
+    __shared__ int32_t chosen_pages[kMaxChosenPages];
+    int64_t eq_run = eq_before, rank = chosen_before;
+    for (int64_t base = w_lo; base < w_hi; base += 32) {
+      unsigned eq_mask;
+      const int64_t pg = base + lane;
+      const bool t = HS_TAKE(pg, eq_run, eq_mask);
+      const unsigned t_mask = __ballot_sync(kFullMask, t);
+      if (t) chosen_pages[rank + __popc(t_mask & before_me)] = (int32_t)pg;
+      rank += __popc(t_mask);
+      eq_run += __popc(eq_mask);
+    }
+    __syncthreads();
+    const int64_t P = p.page_size, tokens = chosen_total * P;
+    for (int64_t t = tid; t < tokens; t += blockDim.x) {
+      const int64_t tok = (int64_t)chosen_pages[t / P] * P + t % P;
+      out[t] = tok < length ? (int32_t)tok : -1;  // only the tail page is partial
+    }
+  } else {
+    int64_t eq_run = eq_before, rank = chosen_before;
+    for (int64_t base = w_lo; base < w_hi; base += 32) {
+      unsigned eq_mask;
+      const int64_t pg = base + lane;
+      const bool t = HS_TAKE(pg, eq_run, eq_mask);
+      const unsigned t_mask = __ballot_sync(kFullMask, t);
+      if (t) {
+        const int64_t r = rank + __popc(t_mask & before_me);
         const int64_t first = pg * p.page_size;
         const int64_t cnt = min((int64_t)p.page_size, length - first);
-        for (int64_t i = 0; i < cnt; ++i) out[rank * p.page_size + i] = (int32_t)(first + i);
-        ++rank;
+        for (int64_t i = 0; i < cnt; ++i) out[r * p.page_size + i] = (int32_t)(first + i);
       }
+      rank += __popc(t_mask);
+      eq_run += __popc(eq_mask);
     }
   }
+#undef HS_TAKE
   // only the tail page (always chosen, always last) can be partial
   const int64_t count = (chosen_total - 1) * p.page_size + (length - (n - 1) * p.page_size);
   for (int64_t i = count + tid; i < p.capacity; i += blockDim.x) out[i] = -1;
@@ -616,7 +670,7 @@ done:
 // bit (0 + s = s, and the same division).
 constexpr int kSelectThreads = 512;
 
-__global__ void __launch_bounds__(kSelectThreads)
+__global__ void __launch_bounds__(kSelectThreads, 1)
     select_partials_kernel(QuestParams<float, float> p, const float *partials, int shards) {
   extern __shared__ uint32_t key_cache[];
   const int b = blockIdx.x;
