@@ -128,3 +128,59 @@ def test_numa_topology_parsing(tmp_path):
     cpus = pci_local_cpus(0, 0x53, 0, tmp_path)
     assert len(cpus) == 112 and 56 in cpus and 223 in cpus and 0 not in cpus
     assert pci_local_cpus(0, 0x54, 0, tmp_path) is None
+
+
+def test_bench_host_store_budget(monkeypatch):
+    """bench.py sizes each rank's pinned host store to half the free host RAM
+    shared by the node's ranks, and refuses when not even four pages' worth
+    of contexts fit."""
+    import bench
+
+    page = 64 * 1024
+    wanted = 16 * 32 * 2048  # configuration 2: REQUESTS x LAYERS x pages
+    monkeypatch.setattr(bench, "available_host_bytes", lambda: 1 << 40)  # 1 TiB free
+    monkeypatch.setenv("LOCAL_WORLD_SIZE", "1")
+    assert bench.host_store_pages(wanted, page, lambda m: None) == wanted
+    monkeypatch.setenv("LOCAL_WORLD_SIZE", "8")
+    monkeypatch.setattr(bench, "available_host_bytes", lambda: 1 << 39)  # 512 GiB free
+    shared = bench.host_store_pages(wanted, page, lambda m: None)
+    assert shared == (1 << 39) // 2 // 8 // page < wanted
+    monkeypatch.setattr(bench, "available_host_bytes", lambda: None)  # unknown: no cap
+    assert bench.host_store_pages(wanted, page, lambda m: None) == wanted
+    monkeypatch.setattr(bench, "available_host_bytes", lambda: 1 << 30)
+    with pytest.raises(RuntimeError, match="host RAM"):
+        bench.host_store_pages(wanted, page, lambda m: None)
+
+
+def test_bench_clock_window(tmp_path):
+    """Clock samples are kept for the timed window; throttle reasons are
+    collected from the samples inside it."""
+    import datetime
+    import time
+
+    import bench
+
+    sampler = bench.ClockSampler(0)
+    sampler.path = tmp_path / "clocks.csv"
+    now = time.time()
+    lines = []
+    for k in range(12):
+        stamp = datetime.datetime.fromtimestamp(now - 0.6 + 0.1 * k).strftime(
+            "%Y/%m/%d %H:%M:%S.%f")[:-3]
+        reason = "Active" if k == 3 else "Not Active"   # before the window
+        lines.append(f"{stamp}, 0, {1900 + k}, 1965, 700.0, 0x0, Not Active, Not Active, "
+                     f"Not Active, {reason}")
+    sampler.path.write_text("\n".join(lines))
+
+    class Done:
+        def terminate(self):
+            pass
+
+        def wait(self, timeout=None):
+            pass
+
+    sampler.proc = Done()
+    sampler.window(now - 0.05, now + 0.25)
+    clocks = sampler.stop()
+    assert clocks["window"] == "timed region" and clocks["samples"] >= 3
+    assert clocks["reasons"] == [] and clocks["sm_max_mhz"] == 1965.0
