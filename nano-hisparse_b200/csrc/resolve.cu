@@ -13,10 +13,14 @@
 //   5. a stable 4-way partition of the old LRU order by category
 //      (untouched, inserted, protected, inserted+protected) is the new LRU;
 //   6. inputs map back to their first occurrence in input order.
-// Per-request scratch lives in shared memory when it fits, else in the
-// caller's workspace (L2-resident); the code is the same through generic
-// pointers. No host round trip: the launch is graph-capturable.
+// Per-request scratch lives in one CTA's shared memory when it fits; when it
+// does not (e.g. 8192 positions against 16384 hot rows, ~660 KiB), a cluster
+// of up to 8 CTAs holds it in distributed shared memory; beyond that it lives
+// in the caller's workspace (L2-resident). The same code runs in all three
+// through the scratch policy (LocalScratch / ClusterScratch). No host round
+// trip: the launch is graph-capturable.
 #include <cstdio>
+#include <mutex>
 
 #include "common.cuh"
 
@@ -92,8 +96,9 @@ __device__ __forceinline__ uint32_t hash_slot(uint32_t key, int64_t ch) {
   return (uint32_t)((key * 0x9E3779B1u) & (uint32_t)(ch - 1));
 }
 
-__device__ __forceinline__ void hash_insert(unsigned long long *table, int64_t ch,
-                                            uint32_t key, uint32_t slot) {
+template <typename Table>
+__device__ __forceinline__ void hash_insert(const Table &table, int64_t ch, uint32_t key,
+                                            uint32_t slot) {
   const unsigned long long entry = ((unsigned long long)key << 32) | slot;
   uint32_t h = hash_slot(key, ch);
   while (true) {
@@ -110,8 +115,8 @@ __device__ __forceinline__ void hash_insert(unsigned long long *table, int64_t c
   }
 }
 
-__device__ __forceinline__ int hash_find(const unsigned long long *table, int64_t ch,
-                                         uint32_t key) {
+template <typename Table>
+__device__ __forceinline__ int hash_find(const Table &table, int64_t ch, uint32_t key) {
   uint32_t h = hash_slot(key, ch);
   while (true) {
     const unsigned long long cur = table[h];
@@ -128,7 +133,8 @@ __device__ __forceinline__ int64_t load_position(const ResolveParams &p, int b, 
 }
 
 // Smallest j in [0, n) with keys[j] >= v (n if none).
-__device__ __forceinline__ int lower_bound(const int32_t *keys, int n, int64_t v) {
+template <typename Keys>
+__device__ __forceinline__ int lower_bound(const Keys &keys, int n, int64_t v) {
   int lo = 0, hi = n;
   while (lo < hi) {
     const int mid = (lo + hi) >> 1;
@@ -137,20 +143,111 @@ __device__ __forceinline__ int lower_bound(const int32_t *keys, int n, int64_t v
   return lo;
 }
 
+// ---- scratch access --------------------------------------------------------------
+// The per-request scratch (Layout) is one logical byte buffer. LocalScratch is
+// one CTA's view of it (its shared memory, or the workspace in global memory);
+// ClusterScratch spreads it over the shared memory of the CTAs of a thread-
+// block cluster (distributed shared memory: CTA r holds bytes
+// [r << shift, (r + 1) << shift)), so scratch too large for one SM still stays
+// on chip. Both give the thread index and count, the barrier, a block- or
+// cluster-wide OR and exclusive scan, and element addresses.
+struct LocalScratch {
+  char *base;
+  __device__ __forceinline__ int tid() const { return (int)threadIdx.x; }
+  __device__ __forceinline__ int nthreads() const { return (int)blockDim.x; }
+  __device__ __forceinline__ void sync() const { __syncthreads(); }
+  __device__ __forceinline__ bool any(int v) const { return __syncthreads_or(v) != 0; }
+  template <typename T> __device__ __forceinline__ T *at(size_t off) const {
+    return reinterpret_cast<T *>(base + off);
+  }
+  template <typename T> __device__ __forceinline__ T scan(T v, T *scratch, T *total) const {
+    return block_exclusive_scan<T>(v, scratch, total);
+  }
+};
+
+constexpr int kClusterShift = 17;  // 128 KiB of scratch per CTA of a cluster
+constexpr int kMaxCluster = 8;     // portable cluster size
+
+__device__ __forceinline__ void cluster_barrier() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n"
+               "barrier.cluster.wait.acquire.aligned;\n" ::: "memory");
+}
+__device__ __forceinline__ unsigned cluster_rank() {
+  unsigned r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;\n" : "=r"(r));
+  return r;
+}
+// Generic address of `p` (this CTA's shared memory) in the shared memory of CTA
+// `rank` of the cluster.
+template <typename T> __device__ __forceinline__ T *map_rank(T *p, unsigned rank) {
+  uint64_t out;
+  asm volatile("mapa.u64 %0, %1, %2;\n" : "=l"(out) : "l"(reinterpret_cast<uint64_t>(p)),
+               "r"(rank));
+  return reinterpret_cast<T *>(out);
+}
+
+struct ClusterScratch {
+  char *base;                   // this CTA's part
+  unsigned rank, size;          // this CTA's cluster rank, CTAs in the cluster
+  unsigned long long *totals;   // [kMaxCluster] scan totals, in this CTA's shared memory
+  __device__ __forceinline__ int tid() const { return (int)(rank * blockDim.x + threadIdx.x); }
+  __device__ __forceinline__ int nthreads() const { return (int)(size * blockDim.x); }
+  __device__ __forceinline__ void sync() const { cluster_barrier(); }
+  template <typename T> __device__ __forceinline__ T *at(size_t off) const {
+    return map_rank(reinterpret_cast<T *>(base + (off & ((size_t(1) << kClusterShift) - 1))),
+                    (unsigned)(off >> kClusterShift));
+  }
+  // Exclusive scan in cluster thread order (rank-major): the block scan, then
+  // each CTA's total is written into every CTA's `totals` and summed in rank order.
+  template <typename T> __device__ __forceinline__ T scan(T v, T *scratch, T *total) const {
+    T block_total;
+    const T prefix = block_exclusive_scan<T>(v, scratch, &block_total);
+    if (threadIdx.x == 0)
+      for (unsigned r = 0; r < size; ++r)
+        *map_rank(totals + rank, r) = (unsigned long long)block_total;
+    cluster_barrier();
+    T before = 0, all = 0;
+    for (unsigned r = 0; r < size; ++r) {
+      const T t = (T)totals[r];
+      all += t;
+      if (r < rank) before += t;
+    }
+    *total = all;
+    cluster_barrier();  // `totals` is rewritten by the next scan
+    return before + prefix;
+  }
+  __device__ __forceinline__ bool any(int v) const {
+    __shared__ unsigned long long any_scratch[33];
+    unsigned long long total;
+    scan<unsigned long long>(v ? 1ull : 0ull, any_scratch, &total);
+    return total != 0;
+  }
+};
+
+template <typename T, typename S> struct Arr {
+  S s;
+  size_t off;
+  __device__ __forceinline__ T &operator[](int64_t i) const {
+    return *s.template at<T>(off + (size_t)i * sizeof(T));
+  }
+};
+
 // Packed counters for one scan: misses in bits 0-20, hot hits 21-41, resident
 // hits 42-62 (count < 2^21, checked on the host).
 constexpr int kCountBits = 21;
 constexpr unsigned long long kCountMask = (1ull << kCountBits) - 1;
 
-// Steps 3-9 of resolve_kernel (every thread of the block calls it).
+// Steps 3-9 of resolve_kernel (every thread of the block or cluster calls it).
+template <typename S>
 __device__ __forceinline__ void resolve_body(const ResolveParams &p, const Layout &L, int b,
-                                          bool sorted, int32_t *keys, int32_t *first_in,
-                                          uint8_t *jflags, int32_t *jslot, int32_t *jrank,
-                                          int64_t *jhost, int64_t *jphys,
-                                          unsigned long long *table, uint8_t *sflags,
-                                          int32_t *lru_old, int32_t *victims,
+                                          bool sorted, const S &sc, Arr<int32_t, S> keys,
+                                          Arr<int32_t, S> first_in, Arr<uint8_t, S> jflags,
+                                          Arr<int32_t, S> jslot, Arr<int32_t, S> jrank,
+                                          Arr<int64_t, S> jhost, Arr<int64_t, S> jphys,
+                                          Arr<unsigned long long, S> table, Arr<uint8_t, S> sflags,
+                                          Arr<int32_t, S> lru_old, Arr<int32_t, S> victims,
                                           unsigned long long *scan_scratch) {
-  const int tid = threadIdx.x, nthreads = blockDim.x;
+  const int tid = sc.tid(), nthreads = sc.nthreads();
   const int K = (int)p.count, H = (int)p.hot_rows;
   const int32_t *src_tab = p.source.at(b);
   const int32_t *res_tab = p.resident.at(b);
@@ -195,7 +292,7 @@ __device__ __forceinline__ void resolve_body(const ResolveParams &p, const Layou
     const int32_t t = tags[s];
     if (t >= 0) hash_insert(table, L.ch, (uint32_t)t, (uint32_t)s);
   }
-  __syncthreads();
+  sc.sync();
   // ---- 4. hot hits; tags wanted by this selection ---------------------------------
   for (int j = tid; j < K; j += nthreads) {
     uint8_t f = jflags[j];
@@ -213,7 +310,7 @@ __device__ __forceinline__ void resolve_body(const ResolveParams &p, const Layou
       jflags[j] = f;
     }
   }
-  __syncthreads();
+  sc.sync();
   // ---- 5. protected slots; packed counts and miss ranks (sorted logical order) ----
   for (int s = tid; s < H; s += nthreads) {
     const int32_t t = tags[s];
@@ -230,7 +327,7 @@ __device__ __forceinline__ void resolve_body(const ResolveParams &p, const Layou
       local += (f & kMiss) ? 1ull : (f & kHotHit) ? (1ull << kCountBits)
                : (f & kResidentHit) ? (1ull << (2 * kCountBits)) : 0ull;
     }
-    unsigned long long prefix = block_exclusive_scan<unsigned long long>(local, scan_scratch,
+    unsigned long long prefix = sc.template scan<unsigned long long>(local, scan_scratch,
                                                                         &totals);
     int rank = (int)(prefix & kCountMask);
     int ready = (int)(((prefix >> kCountBits) & kCountMask) + ((prefix >> (2 * kCountBits)) & kCountMask));
@@ -246,14 +343,14 @@ __device__ __forceinline__ void resolve_body(const ResolveParams &p, const Layou
     unsigned long long local = 0;
     for (int i = hlo; i < hhi; ++i) local += !(sflags[lru_old[i]] & kProtected);
     unsigned long long unprotected;
-    int pos = (int)block_exclusive_scan<unsigned long long>(local, scan_scratch, &unprotected);
+    int pos = (int)sc.template scan<unsigned long long>(local, scan_scratch, &unprotected);
     for (int i = hlo; i < hhi; ++i) {
       const int32_t s = lru_old[i];
       if (!(sflags[s] & kProtected)) victims[pos++] = s;
       else victims[(int)unprotected + (i - pos)] = s;
     }
   }
-  __syncthreads();
+  sc.sync();
   if (misses > H) {
     // only reachable with more positions than hot rows (the cache caps
     // positions at max_union_rows <= hot_rows)
@@ -299,7 +396,7 @@ __device__ __forceinline__ void resolve_body(const ResolveParams &p, const Layou
     out_counts[1] = (int64_t)((totals >> kCountBits) & kCountMask);
     out_counts[2] = misses;
   }
-  __syncthreads();
+  sc.sync();
   // ---- 8. new LRU: stable partition by category of the old order ------------------
   {
     // four 16-bit counters (hot_rows <= 65535, checked on the host)
@@ -310,7 +407,7 @@ __device__ __forceinline__ void resolve_body(const ResolveParams &p, const Layou
       local += 1ull << (16 * cat);
     }
     unsigned long long tot;
-    const unsigned long long e = block_exclusive_scan<unsigned long long>(local, scan_scratch, &tot);
+    const unsigned long long e = sc.template scan<unsigned long long>(local, scan_scratch, &tot);
     const int t0 = (int)(tot & 0xffff), t1 = (int)((tot >> 16) & 0xffff),
               t2 = (int)((tot >> 32) & 0xffff);
     int pos[4] = {(int)(e & 0xffff), t0 + (int)((e >> 16) & 0xffff),
@@ -343,26 +440,18 @@ __device__ __forceinline__ void resolve_body(const ResolveParams &p, const Layou
 }
 
 
-__global__ void __launch_bounds__(kResolveThreads) resolve_kernel(ResolveParams p) {
-  extern __shared__ __align__(16) char smem_raw[];
-  __shared__ unsigned long long scan_scratch[33];
-  __shared__ int s_abort;
-  const int b = blockIdx.x;
-  const int tid = threadIdx.x, nthreads = blockDim.x;
+// Steps 1-2, then the body, for request b (every thread of the block or cluster).
+template <typename S>
+__device__ __forceinline__ void resolve_run(const ResolveParams &p, int b, const S &sc,
+                                         unsigned long long *scan_scratch) {
+  const int tid = sc.tid(), nthreads = sc.nthreads();
   const Layout L(p.count, p.hot_rows);
   const int K = (int)p.count, H = (int)p.hot_rows, KP = (int)L.kp, CH = (int)L.ch;
-  char *base = p.workspace ? p.workspace + (size_t)b * L.total : smem_raw;
-  int32_t *keys = reinterpret_cast<int32_t *>(base + L.keys);
-  int32_t *first_in = reinterpret_cast<int32_t *>(base + L.first);
-  uint8_t *jflags = reinterpret_cast<uint8_t *>(base + L.flags);
-  int32_t *jslot = reinterpret_cast<int32_t *>(base + L.slot);
-  int32_t *jrank = reinterpret_cast<int32_t *>(base + L.rank);
-  int64_t *jhost = reinterpret_cast<int64_t *>(base + L.host);
-  int64_t *jphys = reinterpret_cast<int64_t *>(base + L.phys);
-  unsigned long long *table = reinterpret_cast<unsigned long long *>(base + L.hash);
-  uint8_t *sflags = reinterpret_cast<uint8_t *>(base + L.sflags);
-  int32_t *lru_old = reinterpret_cast<int32_t *>(base + L.lru_old);
-  int32_t *victims = reinterpret_cast<int32_t *>(base + L.victims);
+  const Arr<int32_t, S> keys{sc, L.keys}, first_in{sc, L.first}, jslot{sc, L.slot},
+      jrank{sc, L.rank}, lru_old{sc, L.lru_old}, victims{sc, L.victims};
+  const Arr<uint8_t, S> jflags{sc, L.flags}, sflags{sc, L.sflags};
+  const Arr<int64_t, S> jhost{sc, L.host}, jphys{sc, L.phys};
+  const Arr<unsigned long long, S> table{sc, L.hash};
 
   int64_t *lru = p.lru.at(b);
   const int64_t length = p.lengths.at(b);
@@ -371,7 +460,6 @@ __global__ void __launch_bounds__(kResolveThreads) resolve_kernel(ResolveParams 
   int64_t *out_md = p.out_miss_device + (int64_t)b * K;
   int64_t *out_counts = p.out_counts + (int64_t)b * 3;
 
-  if (tid == 0) s_abort = 0;
   // ---- 1. normalise positions; clear the hash; copy the LRU ---------------------
   for (int i = tid; i < KP; i += nthreads) {
     int32_t v = INT32_MAX;
@@ -382,18 +470,19 @@ __global__ void __launch_bounds__(kResolveThreads) resolve_kernel(ResolveParams 
     keys[i] = v;
   }
   for (int s = tid; s < CH; s += nthreads) table[s] = kEmpty;
-  __syncthreads();
-  int unsorted = 0;
+  sc.sync();
+  int unsorted = 0, corrupt = 0;
   for (int i = tid; i + 1 < KP; i += nthreads) unsorted |= keys[i] > keys[i + 1];
   for (int s = tid; s < H; s += nthreads) {
     sflags[s] = 0;
     const int64_t v = lru[s];
-    if (v < 0 || v >= H) s_abort = 1;
+    if (v < 0 || v >= H) corrupt = 1;
     lru_old[s] = (int32_t)v;
   }
   // ---- 2. sort (skipped for sorted input such as Quest's, whose -1 padding
   //         normalises past the end); first occurrence in input order --------
-  const bool sorted = !__syncthreads_or(unsorted);
+  const bool sorted = !sc.any(unsorted);
+  const bool abort = sc.any(corrupt);
   if (!sorted) {
     for (int i = tid; i < K; i += nthreads) first_in[i] = K;
     for (int k = 2; k <= KP; k <<= 1) {
@@ -409,7 +498,7 @@ __global__ void __launch_bounds__(kResolveThreads) resolve_kernel(ResolveParams 
             }
           }
         }
-        __syncthreads();
+        sc.sync();
       }
     }
     for (int i = tid; i < K; i += nthreads) {
@@ -417,7 +506,7 @@ __global__ void __launch_bounds__(kResolveThreads) resolve_kernel(ResolveParams 
       if (raw >= 0 && raw < length) atomicMin(&first_in[lower_bound(keys, K, raw)], i);
     }
   }
-  if (s_abort) {
+  if (abort) {
     // a corrupt LRU permutation cannot be resolved faithfully: tables stay
     // untouched and the plan is empty
     for (int i = tid; i < K; i += nthreads) out_phys[i] = out_mh[i] = out_md[i] = -1;
@@ -426,17 +515,99 @@ __global__ void __launch_bounds__(kResolveThreads) resolve_kernel(ResolveParams 
     if (tid < 3) out_counts[tid] = 0;
     if (tid == 0) flag(p.status, HS_DEV_LRU_CORRUPT);
   } else {
-    resolve_body(p, L, b, sorted, keys, first_in, jflags, jslot, jrank, jhost, jphys, table,
+    resolve_body(p, L, b, sorted, sc, keys, first_in, jflags, jslot, jrank, jhost, jphys, table,
                  sflags, lru_old, victims, scan_scratch);
   }
   if (p.head_columns != nullptr) {
-    __syncthreads();
+    sc.sync();
     const int64_t n = p.head_count * p.head_width;
     for (int64_t i = tid; i < n; i += nthreads) {
       const int64_t c = p.head_columns[i];
       p.out_head_physical[i] = (c >= 0 && c < K) ? out_phys[c] : -1;
     }
   }
+}
+
+// One CTA per request; scratch in its shared memory or in the workspace.
+__global__ void __launch_bounds__(kResolveThreads) resolve_kernel(ResolveParams p) {
+  extern __shared__ __align__(16) char smem_raw[];
+  __shared__ unsigned long long scan_scratch[33];
+  const int b = blockIdx.x;
+  const Layout L(p.count, p.hot_rows);
+  const LocalScratch sc{p.workspace ? p.workspace + (size_t)b * L.total : smem_raw};
+  resolve_run(p, b, sc, scan_scratch);
+}
+
+// One cluster of `size` CTAs per request; the scratch spread over their shared
+// memory. Every thread of every CTA reaches the same cluster barriers (no path
+// returns early), including one before any remote access and one before exit.
+__global__ void __launch_bounds__(kResolveThreads, 1) resolve_cluster_kernel(ResolveParams p) {
+  extern __shared__ __align__(16) char smem_raw[];
+  __shared__ unsigned long long scan_scratch[33];
+  __shared__ unsigned long long totals[kMaxCluster];
+  unsigned size;
+  asm volatile("mov.u32 %0, %%cluster_nctarank;\n" : "=r"(size));
+  const unsigned rank = cluster_rank();
+  const int b = (int)(blockIdx.x / size);
+  const ClusterScratch sc{smem_raw, rank, size, totals};
+  cluster_barrier();  // every CTA of the cluster runs before its shared memory is touched
+  resolve_run(p, b, sc, scan_scratch);
+  cluster_barrier();  // no CTA exits while another may still use its shared memory
+}
+
+// Whether clusters of `size` resolver CTAs (1024 threads, 128 KiB of shared
+// memory each) fit the device, asked once per device and size.
+bool cluster_schedulable(int size) {
+  static std::mutex lock;
+  static signed char known[64][kMaxCluster + 1];  // 0 unknown, 1 yes, -1 no
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return false;
+  std::lock_guard<std::mutex> guard(lock);
+  if (known[dev][size] != 0) return known[dev][size] > 0;
+  bool ok = reserve_smem((const void *)resolve_cluster_kernel, size_t(1) << kClusterShift,
+                         "resolve") == HS_OK;
+  if (ok) {
+    cudaLaunchConfig_t config{};
+    config.gridDim = dim3((unsigned)size);
+    config.blockDim = dim3(kResolveThreads);
+    config.dynamicSmemBytes = size_t(1) << kClusterShift;
+    cudaLaunchAttribute attr{};
+    attr.id = cudaLaunchAttributeClusterDimension;
+    attr.val.clusterDim.x = (unsigned)size;
+    attr.val.clusterDim.y = 1;
+    attr.val.clusterDim.z = 1;
+    config.attrs = &attr;
+    config.numAttrs = 1;
+    int clusters = 0;
+    ok = cudaOccupancyMaxActiveClusters(&clusters, (const void *)resolve_cluster_kernel,
+                                        &config) == cudaSuccess &&
+         clusters > 0;
+    cudaGetLastError();
+  }
+  known[dev][size] = ok ? 1 : -1;
+  return ok;
+}
+
+int launch_cluster(const ResolveParams &p, int size, cudaStream_t stream) {
+  cudaLaunchConfig_t config{};
+  config.gridDim = dim3((unsigned)(p.batch * size));
+  config.blockDim = dim3(kResolveThreads);
+  config.dynamicSmemBytes = size_t(1) << kClusterShift;
+  config.stream = stream;
+  cudaLaunchAttribute attr{};
+  attr.id = cudaLaunchAttributeClusterDimension;
+  attr.val.clusterDim.x = (unsigned)size;
+  attr.val.clusterDim.y = 1;
+  attr.val.clusterDim.z = 1;
+  config.attrs = &attr;
+  config.numAttrs = 1;
+  const cudaError_t err = cudaLaunchKernelEx(&config, resolve_cluster_kernel, p);
+  if (err != cudaSuccess) {
+    cudaGetLastError();
+    return set_error(HS_ERR_CUDA, "resolve_cluster_kernel: launch failed: %s",
+                     cudaGetErrorString(err));
+  }
+  return HS_OK;
 }
 
 int resolve_common(ResolveParams &p, size_t workspace_bytes, cudaStream_t stream) {
@@ -460,6 +631,15 @@ int resolve_common(ResolveParams &p, size_t workspace_bytes, cudaStream_t stream
   if (L.total <= kResolveSmemLimit) {
     smem = L.total;
     p.workspace = nullptr;
+  } else if (L.total <= ((size_t)kMaxCluster << kClusterShift)) {
+    // too large for one SM: a cluster keeps the scratch in distributed shared
+    // memory (no workspace read or written)
+    const int size = (int)((L.total + (size_t(1) << kClusterShift) - 1) >> kClusterShift);
+    if (cluster_schedulable(size)) return launch_cluster(p, size, stream);
+    const size_t need = hs_resolve_workspace_bytes(p.batch, p.count, p.hot_rows);
+    if (!p.workspace || workspace_bytes < need)
+      return set_error(HS_ERR_WORKSPACE, "resolve: workspace of %zu bytes < required %zu",
+                       workspace_bytes, need);
   } else {
     const size_t need = hs_resolve_workspace_bytes(p.batch, p.count, p.hot_rows);
     if (!p.workspace || workspace_bytes < need)
