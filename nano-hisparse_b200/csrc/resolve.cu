@@ -147,9 +147,9 @@ __device__ __forceinline__ int lower_bound(const Keys &keys, int n, int64_t v) {
 // The per-request scratch (Layout) is one logical byte buffer. LocalScratch is
 // one CTA's view of it (its shared memory, or the workspace in global memory);
 // ClusterScratch spreads it over the shared memory of the CTAs of a thread-
-// block cluster (distributed shared memory: CTA r holds bytes
-// [r << shift, (r + 1) << shift)), so scratch too large for one SM still stays
-// on chip. Both give the thread index and count, the barrier, a block- or
+// block cluster (distributed shared memory), 4 KiB granules dealt round-robin
+// to the CTAs, so scratch too large for one SM still stays on chip and every
+// array's traffic is shared by all the cluster's SMs. Both give the thread index and count, the barrier, a block- or
 // cluster-wide OR and exclusive scan, and element addresses.
 struct LocalScratch {
   char *base;
@@ -165,8 +165,9 @@ struct LocalScratch {
   }
 };
 
-constexpr int kClusterShift = 17;  // 128 KiB of scratch per CTA of a cluster
-constexpr int kMaxCluster = 8;     // portable cluster size
+constexpr int kClusterShift = 17;   // 128 KiB of scratch per CTA of a cluster
+constexpr int kMaxCluster = 8;      // portable cluster size (a power of two is used)
+constexpr int kGranuleShift = 12;   // 4 KiB granules dealt round-robin to the CTAs
 
 __device__ __forceinline__ void cluster_barrier() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n"
@@ -188,14 +189,17 @@ template <typename T> __device__ __forceinline__ T *map_rank(T *p, unsigned rank
 
 struct ClusterScratch {
   char *base;                   // this CTA's part
-  unsigned rank, size;          // this CTA's cluster rank, CTAs in the cluster
+  unsigned rank, size;          // this CTA's cluster rank, CTAs in the cluster (power of 2)
+  unsigned size_log2;
   unsigned long long *totals;   // [kMaxCluster] scan totals, in this CTA's shared memory
   __device__ __forceinline__ int tid() const { return (int)(rank * blockDim.x + threadIdx.x); }
   __device__ __forceinline__ int nthreads() const { return (int)(size * blockDim.x); }
   __device__ __forceinline__ void sync() const { cluster_barrier(); }
   template <typename T> __device__ __forceinline__ T *at(size_t off) const {
-    return map_rank(reinterpret_cast<T *>(base + (off & ((size_t(1) << kClusterShift) - 1))),
-                    (unsigned)(off >> kClusterShift));
+    const size_t granule = off >> kGranuleShift;
+    const size_t local = ((granule >> size_log2) << kGranuleShift) |
+                         (off & ((size_t(1) << kGranuleShift) - 1));
+    return map_rank(reinterpret_cast<T *>(base + local), (unsigned)(granule & (size - 1)));
   }
   // Exclusive scan in cluster thread order (rank-major): the block scan, then
   // each CTA's total is written into every CTA's `totals` and summed in rank order.
@@ -549,7 +553,7 @@ __global__ void __launch_bounds__(kResolveThreads, 1) resolve_cluster_kernel(Res
   asm volatile("mov.u32 %0, %%cluster_nctarank;\n" : "=r"(size));
   const unsigned rank = cluster_rank();
   const int b = (int)(blockIdx.x / size);
-  const ClusterScratch sc{smem_raw, rank, size, totals};
+  const ClusterScratch sc{smem_raw, rank, size, (unsigned)(__ffs((int)size) - 1), totals};
   cluster_barrier();  // every CTA of the cluster runs before its shared memory is touched
   resolve_run(p, b, sc, scan_scratch);
   cluster_barrier();  // no CTA exits while another may still use its shared memory
@@ -634,7 +638,8 @@ int resolve_common(ResolveParams &p, size_t workspace_bytes, cudaStream_t stream
   } else if (L.total <= ((size_t)kMaxCluster << kClusterShift)) {
     // too large for one SM: a cluster keeps the scratch in distributed shared
     // memory (no workspace read or written)
-    const int size = (int)((L.total + (size_t(1) << kClusterShift) - 1) >> kClusterShift);
+    int size = 2;  // a power of two: granules are dealt with masks and shifts
+    while (((size_t)size << kClusterShift) < L.total) size <<= 1;
     if (cluster_schedulable(size)) return launch_cluster(p, size, stream);
     const size_t need = hs_resolve_workspace_bytes(p.batch, p.count, p.hot_rows);
     if (!p.workspace || workspace_bytes < need)
