@@ -115,6 +115,27 @@ template <typename T> __device__ __forceinline__ T warp_inclusive_scan(T v) {
   return v;
 }
 
+// ---- thread-block clusters -----------------------------------------------------
+// Barrier over every thread of every CTA of the cluster; orders the shared-
+// memory writes before it (release) with the reads after it (acquire).
+__device__ __forceinline__ void cluster_barrier() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n"
+               "barrier.cluster.wait.acquire.aligned;\n" ::: "memory");
+}
+__device__ __forceinline__ unsigned cluster_rank() {
+  unsigned r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;\n" : "=r"(r));
+  return r;
+}
+// Generic address of `p` (this CTA's shared memory) in the shared memory of CTA
+// `rank` of the cluster.
+template <typename T> __device__ __forceinline__ T *map_rank(T *p, unsigned rank) {
+  uint64_t out;
+  asm volatile("mapa.u64 %0, %1, %2;\n" : "=l"(out) : "l"(reinterpret_cast<uint64_t>(p)),
+               "r"(rank));
+  return reinterpret_cast<T *>(out);
+}
+
 // Block-wide exclusive scan of one value per thread; returns the exclusive
 // prefix and writes the block total to *total. `scratch` holds >= 33 T.
 // Must be called by every thread of the block.

@@ -25,6 +25,7 @@
 // the products of two 16-bit floats are exact in fp32 and min <= max, so the
 // sums are bit-identical and cost two FFMA per term instead of four ops.
 #include <cstdio>
+#include <mutex>
 
 #include "common.cuh"
 
@@ -139,13 +140,42 @@ struct KeySource {
   }
 };
 
+// One radix step, run by one warp: the digit of the k-th largest key among the
+// keys counted in `h` (256 bins; bins above the digit's width are empty).
+// Lane l owns digits [8*(31-l), 8*(31-l)+7], so the lanes in order walk the
+// digits from the top. Narrows prefix/mask by the digit and leaves in *k the
+// rank of the wanted key among the keys with that digit.
+__device__ __forceinline__ void pick_digit(const uint32_t *h, uint32_t prefix, uint32_t mask,
+                                           int shift, uint32_t digit_mask, uint32_t *s_prefix,
+                                           uint32_t *s_mask, uint32_t *s_k) {
+  const int lane = threadIdx.x & 31;
+  uint32_t local = 0;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) local += h[8 * (31 - lane) + i];
+  const uint32_t inc = warp_inclusive_scan(local);
+  const uint32_t k = *s_k;
+  const unsigned ballot = __ballot_sync(kFullMask, inc >= k);
+  const int owner = __ffs(ballot) - 1;
+  if (lane == owner) {
+    uint32_t above = inc - local;
+    int digit = 8 * (31 - lane) + 7;
+    for (; digit > 8 * (31 - lane); --digit) {
+      if (above + h[digit] >= k) break;
+      above += h[digit];
+    }
+    *s_k = k - above;
+    *s_prefix = prefix | ((uint32_t)digit << shift);
+    *s_mask = mask | (digit_mask << shift);
+  }
+}
+
 // ---- top-k + expansion for one request (run by the last CTA) ------------------
 template <typename TQ, typename TKV>
 __device__ void select_request(const QuestParams<TQ, TKV> &p, int b, int64_t length, int64_t n,
                                uint32_t *key_cache) {
   __shared__ uint32_t hist[256];
   __shared__ int64_t scan_scratch[33];
-  __shared__ uint32_t s_prefix, s_mask, s_k;
+  __shared__ uint32_t s_prefix, s_mask, s_k, s_lo, s_hi;
   const int tid = threadIdx.x;
   int32_t *out = p.out_tokens + (int64_t)b * p.capacity;
   if (length <= 0 || n > p.max_pages) {
@@ -180,52 +210,75 @@ __device__ void select_request(const QuestParams<TQ, TKV> &p, int b, int64_t len
     }
     key_of.cached = key_cache;
   }
+  // The forced pages (key kForcedKey: the tail, and the sink when kept) are
+  // always chosen, so the radix select ranks only the other pages, for the
+  // rest of the budget, and starts at the highest bit in which their keys
+  // differ: the scores of one request share their sign and most exponent
+  // bits, and a digit over those bits sends every page to one histogram bin
+  // (every atomic on one shared-memory word).
+  constexpr uint32_t kForcedKey = 0xffffffffu;  // no score maps here (NaN: 0xfffffffe)
+  const int forced = sink ? 2 : 1;
+  const int lane = tid & 31, warp = tid >> 5, warps = (int)(blockDim.x >> 5);
   if (tid == 0) {
-    s_prefix = 0;
-    s_mask = 0;
-    s_k = (uint32_t)p.top_pages;
+    s_lo = 0xffffffffu;
+    s_hi = 0u;
   }
   __syncthreads();
-  for (int shift = 24; shift >= 0; shift -= 8) {
+  {
+    uint32_t lo = 0xffffffffu, hi = 0u;
+    for (int64_t pg = tid; pg < n; pg += blockDim.x) {
+      const uint32_t key = key_of(pg);
+      if (key != kForcedKey) {
+        lo = min(lo, key);
+        hi = max(hi, key);
+      }
+    }
+    lo = __reduce_min_sync(kFullMask, lo);
+    hi = __reduce_max_sync(kFullMask, hi);
+    if (lane == 0) {
+      atomicMin(&s_lo, lo);
+      atomicMax(&s_hi, hi);
+    }
+  }
+  __syncthreads();
+  // budget left after the forced pages; fewer than the unforced pages (n > top_pages)
+  const uint32_t rest = (uint32_t)(p.top_pages - forced);
+  const uint32_t differ = s_lo ^ s_hi;
+  const int top_bit = differ ? 31 - __clz((int)differ) : -1;
+  if (tid == 0) {
+    // the bits above top_bit are the same in every unforced key
+    const uint32_t common =
+        top_bit < 0 ? 0xffffffffu : top_bit < 31 ? ~((2u << top_bit) - 1u) : 0u;
+    s_prefix = s_hi & common;
+    s_mask = common;
+    s_k = rest;
+  }
+  __syncthreads();
+  for (int high = rest > 0 ? top_bit : -1; high >= 0; high -= 8) {
+    const int shift = high >= 7 ? high - 7 : 0;
+    const uint32_t digit_mask = (2u << (high - shift)) - 1u;  // up to 8 bits
     for (int i = tid; i < 256; i += blockDim.x) hist[i] = 0;
     __syncthreads();
     const uint32_t prefix = s_prefix, mask = s_mask;
     for (int64_t pg = tid; pg < n; pg += blockDim.x) {
       const uint32_t key = key_of(pg);
-      if ((key & mask) == prefix) atomicAdd(&hist[(key >> shift) & 0xffu], 1u);
+      if (key != kForcedKey && (key & mask) == prefix)
+        atomicAdd(&hist[(key >> shift) & digit_mask], 1u);
     }
     __syncthreads();
-    if (tid < 32) {
-      // lane l owns digits [8*(31-l), 8*(31-l)+7]: lanes in order walk digits from the top
-      uint32_t local = 0;
-#pragma unroll
-      for (int i = 0; i < 8; ++i) local += hist[8 * (31 - tid) + i];
-      const uint32_t inc = warp_inclusive_scan(local);
-      const uint32_t k = s_k;
-      const unsigned ballot = __ballot_sync(kFullMask, inc >= k);
-      const int owner = __ffs(ballot) - 1;
-      if (tid == owner) {
-        uint32_t above = inc - local;
-        int digit = 8 * (31 - tid) + 7;
-        for (; digit > 8 * (31 - tid); --digit) {
-          if (above + hist[digit] >= k) break;
-          above += hist[digit];
-        }
-        s_k = k - above;
-        s_prefix = prefix | ((uint32_t)digit << shift);
-        s_mask = mask | (0xffu << shift);
-      }
-    }
+    if (tid < 32) pick_digit(hist, prefix, mask, shift, digit_mask, &s_prefix, &s_mask, &s_k);
     __syncthreads();
   }
-  const uint32_t threshold = s_prefix;
-  const int64_t take_equal = s_k;  // keys == threshold to keep, lowest pages first
+  // rest == 0: the forced pages alone (threshold = their key, all of them
+  // kept); else every key above the threshold, forced pages included, and the
+  // first take_equal keys equal to it
+  const uint32_t threshold = rest > 0 ? s_prefix : kForcedKey;
+  const int64_t take_equal = rest > 0 ? (int64_t)s_k : forced;  // lowest pages first
   // Keep every key above the threshold and the first take_equal keys equal to
   // it, in page order. Warp-major: warp w owns the pages [w*span, (w+1)*span)
   // (span a multiple of 32) and walks them 32 at a time with lane = page, so
   // the shared-memory key reads are consecutive; ballots give each lane the
   // number of equal and of chosen pages before it.
-  const int lane = tid & 31, warp = tid >> 5, warps = (int)(blockDim.x >> 5);
   const unsigned before_me = (1u << lane) - 1u;
   const int64_t span = ceil_div(ceil_div(n, (int64_t)warps), 32) * 32;
   const int64_t w_lo = min(n, warp * span), w_hi = min(n, w_lo + span);
@@ -278,9 +331,11 @@ __device__ void select_request(const QuestParams<TQ, TKV> &p, int b, int64_t len
       eq_run += __popc(eq_mask);
     }
     __syncthreads();
-    const int64_t P = p.page_size, tokens = chosen_total * P;
-    for (int64_t t = tid; t < tokens; t += blockDim.x) {
-      const int64_t tok = (int64_t)chosen_pages[t / P] * P + t % P;
+    // 32-bit index arithmetic: max_pages * page_size <= INT32_MAX (host check)
+    const uint32_t P = (uint32_t)p.page_size, tokens = (uint32_t)chosen_total * P;
+    for (uint32_t t = tid; t < tokens; t += blockDim.x) {
+      const uint32_t r = t / P;
+      const int64_t tok = (int64_t)chosen_pages[r] * P + (t - r * P);
       out[t] = tok < length ? (int32_t)tok : -1;  // only the tail page is partial
     }
   } else {
@@ -703,6 +758,292 @@ __global__ void __launch_bounds__(kSelectThreads, 1)
   select_request(p, b, length, n, n <= kSmemKeys ? key_cache : nullptr);
 }
 
+// ---- cluster select: one request's top-k spread over a thread-block cluster -----
+//
+// For long requests the single-CTA selection above is latency-bound (one SM
+// walks every page several times). Here a cluster of kSelectCluster CTAs
+// shares one request: CTA r owns a contiguous chunk of its pages (a multiple
+// of 32), turns the shard partials into keys in its shared memory (the same
+// shard-ordered fp32 sum and division as select_partials_kernel), and each
+// radix pass counts the chunk into a local histogram that every CTA then sums
+// over the cluster through distributed shared memory, so all CTAs take the
+// same digit. The final walk needs only per-CTA totals of keys above and equal
+// to the threshold: the chosen pages before any position are those above it
+// plus min(equal ones before it, take_equal). Same selection and token order
+// as select_request, bit for bit.
+//
+// Every CTA of a cluster takes the same branch (one request) and so reaches
+// the same cluster barriers: one before the first remote read, one per radix
+// pass (histograms double-buffered, so a pass never clears a buffer a peer may
+// still read), one before the CTA totals are read, one before exit.
+constexpr int kSelectCluster = 8;                 // CTAs per request (portable cluster size)
+constexpr int kClusterSelectThreads = 512;
+constexpr int64_t kClusterSelectMinPages = 4096;  // shorter tables: one CTA is as fast
+constexpr int64_t kClusterChunkMax = 8192;        // pages per CTA: 32 KiB keys + 32 KiB chosen
+
+__global__ void __launch_bounds__(kClusterSelectThreads, 1)
+    select_cluster_kernel(QuestParams<float, float> p, const float *partials, int shards,
+                          int64_t chunk_cap) {
+  extern __shared__ __align__(16) uint32_t cs_keys[];  // [chunk_cap] keys, [chunk_cap] chosen
+  __shared__ uint32_t hist[2][256];
+  __shared__ uint32_t ghist[256];
+  __shared__ int64_t scan_scratch[33];
+  __shared__ uint32_t s_lo, s_hi, g_lo, g_hi, s_prefix, s_mask, s_k;
+  __shared__ long long s_eq_total, s_gt_total;  // this CTA's counts, read by the peers
+  __shared__ long long s_eq_before, s_gt_before;
+  constexpr uint32_t kForcedKey = 0xffffffffu;
+  const unsigned S = kSelectCluster, rank = cluster_rank();
+  const int b = (int)(blockIdx.x / S);
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, warps = (int)(blockDim.x >> 5);
+  const int64_t ctid = (int64_t)rank * blockDim.x + tid, cthreads = (int64_t)S * blockDim.x;
+  const int64_t length = p.lengths.at(b);
+  const int64_t n = length > 0 ? ceil_div(length, (int64_t)p.page_size) : 0;
+  const int64_t P = p.page_size;
+  int32_t *out = p.out_tokens + (int64_t)b * p.capacity;
+  if (length <= 0 || n > p.max_pages || p.top_pages >= n) {
+    // no ranking (same results as select_request); no shared memory is shared
+    const bool all = length > 0 && n <= p.max_pages;
+    if (n > p.max_pages && ctid == 0) flag(p.status, HS_DEV_PAGES_EXCEED_TABLE);
+    for (int64_t i = ctid; i < p.capacity; i += cthreads)
+      out[i] = all && i < length ? (int32_t)i : -1;
+    if (ctid == 0) p.out_counts[b] = all ? (int32_t)length : 0;
+    return;
+  }
+  const bool sink = p.keep_sink && p.top_pages > 1 && n > 1;
+  const int forced = sink ? 2 : 1;
+  const int64_t chunk = ceil_div(ceil_div(n, (int64_t)S), (int64_t)32) * 32;  // <= chunk_cap
+  const int64_t c_lo = min(n, (int64_t)rank * chunk), c_len = min(n, c_lo + chunk) - c_lo;
+  uint32_t *keys = cs_keys;
+  int32_t *chosen = reinterpret_cast<int32_t *>(cs_keys + chunk_cap);
+  if (tid == 0) {
+    s_lo = 0xffffffffu;
+    s_hi = 0u;
+  }
+  __syncthreads();
+  {
+    uint32_t lo = 0xffffffffu, hi = 0u;
+    for (int64_t i0 = tid; i0 < c_len; i0 += 4 * (int64_t)blockDim.x) {
+      float total[4] = {0.f, 0.f, 0.f, 0.f};
+      for (int r = 0; r < shards; ++r) {
+        const float *row = partials + ((int64_t)r * p.batch + b) * p.max_pages + c_lo;
+        float v[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int64_t i = i0 + (int64_t)u * blockDim.x;
+          v[u] = i < c_len ? __ldcg(row + i) : 0.f;
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) total[u] = __fadd_rn(total[u], v[u]);
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int64_t i = i0 + (int64_t)u * blockDim.x, pg = c_lo + i;
+        if (i < c_len) {
+          const bool is_forced = pg == n - 1 || (sink && pg == 0);
+          const uint32_t key =
+              is_forced ? kForcedKey : score_key(__fdiv_rn(total[u], (float)p.q_heads));
+          keys[i] = key;
+          if (!is_forced) {
+            lo = min(lo, key);
+            hi = max(hi, key);
+          }
+        }
+      }
+    }
+    lo = __reduce_min_sync(kFullMask, lo);
+    hi = __reduce_max_sync(kFullMask, hi);
+    if (lane == 0) {
+      atomicMin(&s_lo, lo);
+      atomicMax(&s_hi, hi);
+    }
+  }
+  cluster_barrier();  // keys and every CTA's key range are complete
+  if (tid == 0) {
+    uint32_t lo = 0xffffffffu, hi = 0u;
+    for (unsigned r = 0; r < S; ++r) {
+      lo = min(lo, *map_rank(&s_lo, r));
+      hi = max(hi, *map_rank(&s_hi, r));
+    }
+    g_lo = lo;
+    g_hi = hi;
+  }
+  __syncthreads();
+  const uint32_t rest = (uint32_t)(p.top_pages - forced);  // < the unforced pages
+  const uint32_t differ = g_lo ^ g_hi;
+  const int top_bit = differ ? 31 - __clz((int)differ) : -1;
+  if (tid == 0) {
+    const uint32_t common =
+        top_bit < 0 ? 0xffffffffu : top_bit < 31 ? ~((2u << top_bit) - 1u) : 0u;
+    s_prefix = g_hi & common;
+    s_mask = common;
+    s_k = rest;
+  }
+  __syncthreads();
+  int pass = 0;
+  for (int high = rest > 0 ? top_bit : -1; high >= 0; high -= 8, ++pass) {
+    const int shift = high >= 7 ? high - 7 : 0;
+    const uint32_t digit_mask = (2u << (high - shift)) - 1u;
+    uint32_t *h = hist[pass & 1];
+    for (int i = tid; i < 256; i += blockDim.x) h[i] = 0;
+    __syncthreads();
+    const uint32_t prefix = s_prefix, mask = s_mask;
+    for (int64_t i = tid; i < c_len; i += blockDim.x) {
+      const uint32_t key = keys[i];
+      if (key != kForcedKey && (key & mask) == prefix)
+        atomicAdd(&h[(key >> shift) & digit_mask], 1u);
+    }
+    cluster_barrier();  // every CTA's histogram of this pass is complete
+    for (int d = tid; d < 256; d += blockDim.x) {
+      uint32_t sum = 0;
+      for (unsigned r = 0; r < S; ++r) sum += *map_rank(&h[d], r);
+      ghist[d] = sum;
+    }
+    __syncthreads();
+    if (tid < 32) pick_digit(ghist, prefix, mask, shift, digit_mask, &s_prefix, &s_mask, &s_k);
+    __syncthreads();
+  }
+  const uint32_t threshold = rest > 0 ? s_prefix : kForcedKey;
+  const int64_t take_equal = rest > 0 ? (int64_t)s_k : forced;
+  // per warp: keys equal to and above the threshold in its span of the chunk
+  const unsigned before_me = (1u << lane) - 1u;
+  const int64_t span = ceil_div(ceil_div(c_len, (int64_t)warps), (int64_t)32) * 32;
+  const int64_t w_lo = min(c_len, warp * span), w_hi = min(c_len, w_lo + span);
+  int64_t eq_local = 0, gt_local = 0;
+  for (int64_t base = w_lo; base < w_hi; base += 32) {
+    const int64_t i = base + lane;
+    const uint32_t key = i < w_hi ? keys[i] : 0u;
+    eq_local += __popc(__ballot_sync(kFullMask, i < w_hi && key == threshold));
+    gt_local += __popc(__ballot_sync(kFullMask, i < w_hi && key > threshold));
+  }
+  int64_t eq_cta, gt_cta;
+  const int64_t eq_in = __shfl_sync(
+      kFullMask, block_exclusive_scan<int64_t>(lane == 0 ? eq_local : 0, scan_scratch, &eq_cta),
+      0);
+  const int64_t gt_in = __shfl_sync(
+      kFullMask, block_exclusive_scan<int64_t>(lane == 0 ? gt_local : 0, scan_scratch, &gt_cta),
+      0);
+  if (tid == 0) {
+    s_eq_total = eq_cta;
+    s_gt_total = gt_cta;
+  }
+  cluster_barrier();  // every CTA's totals are published
+  if (tid == 0) {
+    long long eq = 0, gt = 0;
+    for (unsigned r = 0; r < rank; ++r) {
+      eq += *map_rank(&s_eq_total, r);
+      gt += *map_rank(&s_gt_total, r);
+    }
+    s_eq_before = eq;
+    s_gt_before = gt;
+  }
+  __syncthreads();
+  const int64_t eq_cta_before = s_eq_before, gt_cta_before = s_gt_before;
+  const int64_t chosen_cta_before = gt_cta_before + min(eq_cta_before, take_equal);
+  const int64_t chosen_cta =
+      gt_cta_before + gt_cta + min(eq_cta_before + eq_cta, take_equal) - chosen_cta_before;
+  {
+    int64_t eq_run = eq_cta_before + eq_in;
+    int64_t at = gt_cta_before + gt_in + min(eq_run, take_equal) - chosen_cta_before;
+    for (int64_t base = w_lo; base < w_hi; base += 32) {
+      const int64_t i = base + lane;
+      const uint32_t key = i < w_hi ? keys[i] : 0u;
+      const bool eq = i < w_hi && key == threshold;
+      const unsigned eq_mask = __ballot_sync(kFullMask, eq);
+      const bool take = (i < w_hi && key > threshold) ||
+                        (eq && eq_run + __popc(eq_mask & before_me) < take_equal);
+      const unsigned t_mask = __ballot_sync(kFullMask, take);
+      if (take) chosen[at + __popc(t_mask & before_me)] = (int32_t)(c_lo + i);
+      at += __popc(t_mask);
+      eq_run += __popc(eq_mask);
+    }
+  }
+  __syncthreads();
+  // this CTA's chosen pages hold ranks [chosen_cta_before, +chosen_cta) of the selection
+  {
+    const uint32_t Pu = (uint32_t)P, tokens = (uint32_t)chosen_cta * Pu;
+    int32_t *dst = out + chosen_cta_before * P;
+    for (uint32_t t = tid; t < tokens; t += blockDim.x) {
+      const uint32_t r = t / Pu;
+      const int64_t tok = (int64_t)chosen[r] * P + (t - r * Pu);
+      dst[t] = tok < length ? (int32_t)tok : -1;  // only the tail page is partial
+    }
+  }
+  const int64_t count = (int64_t)(p.top_pages - 1) * P + (length - (n - 1) * P);
+  for (int64_t i = count + ctid; i < p.capacity; i += cthreads) out[i] = -1;
+  if (ctid == 0) p.out_counts[b] = (int32_t)count;
+  cluster_barrier();  // no CTA exits while a peer may still read its shared memory
+}
+
+// Whether clusters of kSelectCluster select CTAs with `smem` bytes of dynamic
+// shared memory fit the device; asked once per device (the answer is kept for
+// the largest size that fits).
+bool select_cluster_fits(size_t smem) {
+  static std::mutex lock;
+  static size_t fits[64];  // largest dynamic shared memory known to fit, per device
+  static bool asked[64];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return false;
+  std::lock_guard<std::mutex> guard(lock);
+  if (asked[dev]) return smem <= fits[dev];
+  asked[dev] = true;
+  const size_t most = 2 * (size_t)kClusterChunkMax * sizeof(uint32_t);
+  if (reserve_smem((const void *)select_cluster_kernel, most, "quest select") != HS_OK) {
+    cudaGetLastError();
+    return false;
+  }
+  cudaLaunchConfig_t config{};
+  config.gridDim = dim3((unsigned)kSelectCluster);
+  config.blockDim = dim3(kClusterSelectThreads);
+  config.dynamicSmemBytes = most;
+  cudaLaunchAttribute attr{};
+  attr.id = cudaLaunchAttributeClusterDimension;
+  attr.val.clusterDim.x = (unsigned)kSelectCluster;
+  attr.val.clusterDim.y = 1;
+  attr.val.clusterDim.z = 1;
+  config.attrs = &attr;
+  config.numAttrs = 1;
+  int clusters = 0;
+  const bool ok = cudaOccupancyMaxActiveClusters(&clusters, (const void *)select_cluster_kernel,
+                                                 &config) == cudaSuccess &&
+                  clusters > 0;
+  cudaGetLastError();
+  fits[dev] = ok ? most : 0;
+  return ok && smem <= most;
+}
+
+// Pages per CTA of the cluster select for a table of `max_pages`, or 0 when the
+// single-CTA select is used (short tables, or tables beyond the chunk limit).
+int64_t select_cluster_chunk(int64_t max_pages) {
+  if (max_pages < kClusterSelectMinPages) return 0;
+  const int64_t chunk = ceil_div(ceil_div(max_pages, (int64_t)kSelectCluster), (int64_t)32) * 32;
+  if (chunk > kClusterChunkMax) return 0;
+  return select_cluster_fits(2 * (size_t)chunk * sizeof(uint32_t)) ? chunk : 0;
+}
+
+int launch_select_cluster(const QuestParams<float, float> &p, const float *partials, int shards,
+                          int64_t chunk, cudaStream_t stream) {
+  cudaLaunchConfig_t config{};
+  config.gridDim = dim3((unsigned)(p.batch * kSelectCluster));
+  config.blockDim = dim3(kClusterSelectThreads);
+  config.dynamicSmemBytes = 2 * (size_t)chunk * sizeof(uint32_t);
+  config.stream = stream;
+  cudaLaunchAttribute attr{};
+  attr.id = cudaLaunchAttributeClusterDimension;
+  attr.val.clusterDim.x = (unsigned)kSelectCluster;
+  attr.val.clusterDim.y = 1;
+  attr.val.clusterDim.z = 1;
+  config.attrs = &attr;
+  config.numAttrs = 1;
+  const cudaError_t err =
+      cudaLaunchKernelEx(&config, select_cluster_kernel, p, partials, shards, chunk);
+  if (err != cudaSuccess) {
+    cudaGetLastError();
+    return set_error(HS_ERR_CUDA, "select_cluster_kernel: launch failed: %s",
+                     cudaGetErrorString(err));
+  }
+  return HS_OK;
+}
+
 int launch_select_partials(int shards, const float *partials, int batch, const int32_t *lengths,
                            int q_heads, int64_t max_pages, int page_size, int top_pages,
                            int keep_sink, int32_t *out_tokens, int64_t capacity,
@@ -721,6 +1062,8 @@ int launch_select_partials(int shards, const float *partials, int batch, const i
   p.capacity = capacity;
   p.out_counts = out_counts;
   p.status = status;
+  const int64_t chunk = select_cluster_chunk(max_pages);
+  if (chunk > 0) return launch_select_cluster(p, partials, shards, chunk, stream);
   const size_t smem = (size_t)(max_pages < kSmemKeys ? max_pages : kSmemKeys) * sizeof(uint32_t);
   const int rc = reserve_smem((const void *)select_partials_kernel, smem, "quest select");
   if (rc != HS_OK) return rc;
@@ -868,7 +1211,31 @@ template <typename TQ, typename TKV> int run(const Common &c, cudaStream_t strea
   const bool aligned = c.mn_ptrs != nullptr ||
                        ((reinterpret_cast<uintptr_t>(c.mn) | reinterpret_cast<uintptr_t>(c.mx)) &
                         15) == 0;
-  return launch<TQ, TKV>(p, stream, aligned);
+  // Long tables with few requests: score in partial mode (undivided head sums
+  // into the workspace) and rank over a cluster per request, one wave of CTAs.
+  // One shard's sum is the head sum itself (0 + s = s), so the keys, and the
+  // selection, are those of the fused path bit for bit.
+  const int64_t chunk = p.partial || (int64_t)c.batch * kSelectCluster > sm_count()
+                            ? 0
+                            : select_cluster_chunk(c.max_pages);
+  if (chunk == 0) return launch<TQ, TKV>(p, stream, aligned);
+  p.partial = 1;
+  p.done = nullptr;
+  const int rc = launch<TQ, TKV>(p, stream, aligned);
+  if (rc != HS_OK) return rc;
+  QuestParams<float, float> s{};
+  s.batch = c.batch;
+  s.lengths = c.lengths;
+  s.q_heads = c.q_heads;
+  s.page_size = c.page_size;
+  s.top_pages = c.top_pages;
+  s.keep_sink = c.keep_sink;
+  s.max_pages = c.max_pages;
+  s.out_tokens = c.out_tokens;
+  s.capacity = c.capacity;
+  s.out_counts = c.out_counts;
+  s.status = c.status;
+  return launch_select_cluster(s, p.scores, 1, chunk, stream);
 }
 
 template <typename TQ> int dispatch_kv(const Common &c, cudaStream_t s) {

@@ -169,24 +169,6 @@ constexpr int kClusterShift = 17;   // 128 KiB of scratch per CTA of a cluster
 constexpr int kMaxCluster = 8;      // portable cluster size (a power of two is used)
 constexpr int kGranuleShift = 12;   // 4 KiB granules dealt round-robin to the CTAs
 
-__device__ __forceinline__ void cluster_barrier() {
-  asm volatile("barrier.cluster.arrive.release.aligned;\n"
-               "barrier.cluster.wait.acquire.aligned;\n" ::: "memory");
-}
-__device__ __forceinline__ unsigned cluster_rank() {
-  unsigned r;
-  asm volatile("mov.u32 %0, %%cluster_ctarank;\n" : "=r"(r));
-  return r;
-}
-// Generic address of `p` (this CTA's shared memory) in the shared memory of CTA
-// `rank` of the cluster.
-template <typename T> __device__ __forceinline__ T *map_rank(T *p, unsigned rank) {
-  uint64_t out;
-  asm volatile("mapa.u64 %0, %1, %2;\n" : "=l"(out) : "l"(reinterpret_cast<uint64_t>(p)),
-               "r"(rank));
-  return reinterpret_cast<T *>(out);
-}
-
 struct ClusterScratch {
   char *base;                   // this CTA's part
   unsigned rank, size;          // this CTA's cluster rank, CTAs in the cluster (power of 2)

@@ -131,3 +131,92 @@ def test_batched_matches_single():
         assert counts[i].item() == len(expected)
         row = tokens[i].tolist()
         assert row[:len(expected)] == expected and set(row[len(expected):]) <= {-1}
+
+
+def _select_partials(partials, lengths, q_heads, page_size, top, sink):
+    """hs_quest_select_partials on device partials [shards, batch, max_pages]."""
+    lib = _lib.load()
+    shards, batch, max_pages = partials.shape
+    width = top * page_size
+    tokens = torch.empty(batch, width, dtype=torch.int32, device=DEV)
+    counts = torch.empty(batch, dtype=torch.int32, device=DEV)
+    lens = torch.tensor(lengths, dtype=torch.int32, device=DEV)
+    nbytes = lib.hs_quest_workspace_bytes(batch, max_pages)
+    ws = torch.empty(nbytes, dtype=torch.uint8, device=DEV)
+    _lib.check(lib.hs_quest_select_partials(
+        shards, partials.data_ptr(), batch, lens.data_ptr(), q_heads, max_pages, page_size, top,
+        int(sink), tokens.data_ptr(), width, counts.data_ptr(), ws.data_ptr(), nbytes, 0,
+        torch.cuda.current_stream().cuda_stream))
+    return tokens.cpu().numpy(), counts.cpu().numpy()
+
+
+@pytest.mark.parametrize("top", [1, 2, 3, 128])
+@pytest.mark.parametrize("sink", [True, False])
+def test_long_table_selection_edges(top, sink):
+    """Tables of >= 4096 pages rank over a thread-block cluster per request:
+    chunk edges (5000 pages over 8 CTAs), a tail just past the budget, budgets
+    that hold only the forced pages, all-pages requests, empty requests, ties,
+    NaN and infinities — token for token the oracle's selection."""
+    gen = torch.Generator().manual_seed(top * 2 + sink)
+    shards, q_heads, p, max_pages = 2, 28, 16, 5000
+    lengths = [max_pages * p, 4999 * p - 3, 17, (top + 1) * p - 5, 70000, 0, 3000 * p]
+    partials = torch.randn(shards, len(lengths), max_pages, generator=gen) * 50 + 900
+    partials[:, 3] = torch.randint(0, 3, (shards, max_pages), generator=gen).float()  # ties
+    partials[:, 4, ::97] = float("nan")
+    partials[0, 4, 5::101] = float("inf")
+    partials[1, 4, 7::103] = float("-inf")
+    partials[:, 6] = torch.randn(shards, max_pages, generator=gen)  # mixed signs, -0 below
+    partials[:, 6, 11::50] = -0.0
+    tokens, counts = _select_partials(partials.to(DEV), lengths, q_heads, p, top, sink)
+    part = partials.numpy()
+    for i, length in enumerate(lengths):
+        if length == 0:
+            assert counts[i] == 0 and set(tokens[i].tolist()) == {-1}
+            continue
+        total = np.zeros(max_pages, dtype=np.float32)
+        for r in range(shards):
+            total = (total + part[r, i]).astype(np.float32)
+        scores = (total / np.float32(q_heads)).astype(np.float32)
+        n = -(-length // p)
+        want, count = oracle.quest_select(scores[:n], length, p, top, sink, top * p)
+        assert counts[i] == count, (i, length)
+        assert tokens[i].tolist() == want.tolist(), (i, length)
+    assert not _lib.device_flags(DEV)
+
+
+def test_long_table_batched_matches_oracle():
+    """hs_quest_select_batched with a long table and few requests scores in
+    partial mode and ranks over a cluster: same tokens as the oracle."""
+    gen = torch.Generator().manual_seed(21)
+    hq, hkv, d, p, top, max_pages = 28, 4, 128, 64, 128, 4200
+    lengths = [max_pages * p, 1000, 3000 * p + 5]
+    mins, maxs = [], []
+    query = torch.randn(len(lengths), hq, d, generator=gen).to(torch.bfloat16)
+    for _ in lengths:
+        mn, mx = _metadata(gen, max_pages, hkv, d, torch.bfloat16)
+        mins.append(mn)
+        maxs.append(mx)
+    lib = _lib.load()
+    b, width = len(lengths), top * p
+    dmins = [t.to(DEV) for t in mins]
+    dmaxs = [t.to(DEV) for t in maxs]
+    dq = query.to(DEV)
+    tokens = torch.empty(b, width, dtype=torch.int32, device=DEV)
+    counts = torch.empty(b, dtype=torch.int32, device=DEV)
+    mptr = torch.tensor([t.data_ptr() for t in dmins], dtype=torch.int64, device=DEV)
+    xptr = torch.tensor([t.data_ptr() for t in dmaxs], dtype=torch.int64, device=DEV)
+    lens = torch.tensor(lengths, dtype=torch.int32, device=DEV)
+    nbytes = lib.hs_quest_workspace_bytes(b, max_pages)
+    ws = torch.zeros(nbytes, dtype=torch.uint8, device=DEV)
+    for sink in (True, False):
+        _lib.check(lib.hs_quest_select_batched(
+            b, dq.data_ptr(), hq * d, _lib.HS_BFLOAT16, mptr.data_ptr(), xptr.data_ptr(),
+            _lib.HS_BFLOAT16, lens.data_ptr(), hq, hkv, d, max_pages, p, top, int(sink),
+            tokens.data_ptr(), width, counts.data_ptr(), ws.data_ptr(), nbytes, 0,
+            torch.cuda.current_stream().cuda_stream))
+        for i, length in enumerate(lengths):
+            want = oracle.quest_tokens(query[i], mins[i], maxs[i], length, p, top, sink)
+            assert counts[i].item() == len(want)
+            row = tokens[i].tolist()
+            assert row[:len(want)] == want and set(row[len(want):]) <= {-1}
+    assert not _lib.device_flags(DEV)
