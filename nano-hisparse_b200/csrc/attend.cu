@@ -636,7 +636,93 @@ int launch(AttendParams &p, cudaStream_t stream) {
   return check_launch("attend_split_kernel");
 }
 
+// Merge for small grids (fewer (request, head) pairs than SMs, e.g. one long
+// request): one 256-thread CTA per (request, query head, 32 output elements).
+// Every CTA reduces the global max and the denominator of its head's partials
+// (the same order in each, so the 32-element slices agree); then warp w sums
+// the weighted partials w, w+8, ... with lane = output element, all of a
+// warp's loads (at most 16, coalesced 128-byte rows) issued before their use,
+// and the eight warp sums are added in order.
+constexpr int kNarrowThreads = 256;
+constexpr int kNarrowWarps = kNarrowThreads / 32;
+constexpr int kNarrowPerWarp = 2 * kMaxSplits / kNarrowWarps;  // 16
+
+template <typename TQ>
+__global__ void __launch_bounds__(kNarrowThreads) attend_merge_narrow_kernel(AttendParams p) {
+  __shared__ float weight[2 * kMaxSplits];
+  __shared__ float reduce[kNarrowWarps];
+  __shared__ float result[2];
+  __shared__ float acc_sm[kNarrowWarps][32];
+  const int h = blockIdx.x, b = blockIdx.y, t = threadIdx.x;
+  const int lane = t & 31, warp = t >> 5;
+  const int D = p.head_dim, stride = D + 2, d = blockIdx.z * 32 + lane;
+  const int s0 = p.phase_splits[0], s1 = p.phases > 1 ? p.phase_splits[1] : 0;
+  const int total = s0 + s1;  // <= 2 * kMaxSplits
+  p.phase = 0;
+  const float *base0 = partial_slot(p, b, h, 0);
+  p.phase = 1;
+  const float *base1 = partial_slot(p, b, h, 0);
+  auto partial = [&](int i) {
+    return i < s0 ? base0 + (int64_t)i * stride : base1 + (int64_t)(i - s0) * stride;
+  };
+  float m = -INFINITY, l = 0.f;
+  if (t < total) {
+    const float *part = partial(t);
+    m = part[D];
+    l = part[D + 1];
+  }
+  float mm = warp_max(m);
+  if (lane == 0) reduce[warp] = mm;
+  __syncthreads();
+  if (t == 0) {
+    float v = reduce[0];
+    for (int w = 1; w < kNarrowWarps; ++w) v = fmaxf(v, reduce[w]);
+    result[0] = v;
+  }
+  __syncthreads();
+  mm = result[0];
+  const float w = m == -INFINITY ? 0.f : expf(m - mm);
+  if (t < 2 * kMaxSplits) weight[t] = w;
+  const float dl = warp_xor_tree_sum(w * l);
+  __syncthreads();  // reduce[] is reused below
+  if (lane == 0) reduce[warp] = dl;
+  __syncthreads();
+  if (t == 0) {
+    float v = 0.f;
+    for (int i = 0; i < kNarrowWarps; ++i) v += reduce[i];
+    result[1] = v;
+  }
+  __syncthreads();
+  const float denom = result[1];
+  float v[kNarrowPerWarp];
+#pragma unroll
+  for (int k = 0; k < kNarrowPerWarp; ++k) {
+    const int i = warp + k * kNarrowWarps;
+    v[k] = i < total && d < D ? partial(i)[d] : 0.f;
+  }
+  float acc = 0.f;
+#pragma unroll
+  for (int k = 0; k < kNarrowPerWarp; ++k) {
+    const int i = warp + k * kNarrowWarps;
+    if (i < total && weight[i] != 0.f) acc += weight[i] * v[k];  // empty splits: no weight
+  }
+  acc_sm[warp][lane] = acc;
+  __syncthreads();
+  if (t < 32 && d < D) {
+    float num = 0.f;
+#pragma unroll
+    for (int w2 = 0; w2 < kNarrowWarps; ++w2) num += acc_sm[w2][t];
+    TQ *out = static_cast<TQ *>(p.out) + (int64_t)b * p.out_batch_stride + (int64_t)h * D;
+    out[d] = from_f32<TQ>(denom > 0.f ? num / denom : 0.f);
+  }
+}
+
 template <typename TQ> int launch_merge(AttendParams &p, cudaStream_t stream) {
+  if ((int64_t)p.batch * p.q_heads < sm_count()) {
+    const dim3 grid(p.q_heads, p.batch, (unsigned)ceil_div(p.head_dim, 32));
+    attend_merge_narrow_kernel<TQ><<<grid, kNarrowThreads, 0, stream>>>(p);
+    return check_launch("attend_merge_narrow_kernel");
+  }
   attend_merge_kernel<TQ><<<dim3(p.q_heads, p.batch), kMergeThreads, 0, stream>>>(p);
   return check_launch("attend_merge_kernel");
 }
