@@ -672,33 +672,37 @@ def run_config5(args, rank, world, local_rank, log):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
     timed = counts[settle + warmup:].cpu().numpy()
-    graph_ms = None
-    if world == 1:  # the same steps replayed from one captured graph (no collective to capture)
-        from hisparse_b200.batched import DecodeGraph
+    # the same kind of steps replayed from captured graphs: one graph per step
+    # at N = 1; with a group, two per layer with the all-gather issued between
+    # them (no collective is captured)
+    from hisparse_b200.batched import DecodeGraph
 
-        graph = DecodeGraph([batch], L)
-        gq = torch.randn((warmup + steps, L, 1, hq, D), generator=qgen, device=device,
-                         dtype=torch.float32).to(DTYPE)
-        for s_ in range(warmup):
-            graph.queries[0].copy_(gq[s_])
-            graph.replay()
-        torch.cuda.synchronize(device)
-        g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        g0.record()
-        for s_ in range(warmup, warmup + steps):
-            graph.queries[0].copy_(gq[s_])
-            graph.replay()
-        g1.record()
-        torch.cuda.synchronize(device)
-        graph_ms = g0.elapsed_time(g1)
-        for st in batch.layers:
-            st.ready = st.last_use = None
-        del graph
-    # the headline at N = 1 is the graph replay (the eager loop is bound by the
-    # host's launch rate once the step is short); N > 1 times the eager loop
-    eager_ms = ms
-    if graph_ms is not None:
-        ms = graph_ms
+    graph = DecodeGraph([batch], L)
+    gq = torch.randn((warmup + steps, L, 1, hq, D), generator=qgen, device=device,
+                     dtype=torch.float32).to(DTYPE)
+    for s_ in range(warmup):
+        graph.queries[0].copy_(gq[s_])
+        graph.replay()
+    barrier()
+    g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    g0.record()
+    for s_ in range(warmup, warmup + steps):
+        graph.queries[0].copy_(gq[s_])
+        graph.replay()
+    g1.record()
+    barrier()
+    graph_ms = g0.elapsed_time(g1)
+    if world > 1:
+        t = torch.tensor([graph_ms], dtype=torch.float64, device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        graph_ms = float(t.item())
+    segmented = graph.segmented
+    for st in batch.layers:
+        st.ready = st.last_use = None
+    del graph
+    # the headline is the graph replay (the eager loop is bound by the host's
+    # launch rate once the step is short); the eager loop is reported beside it
+    eager_ms, ms = ms, graph_ms
     # per-stage device time: one more step, each stage alone (CUDA events on its stream)
     timing = []
     extra = torch.randn((L, 1, hq, D), generator=qgen, device=device,
@@ -731,8 +735,8 @@ def run_config5(args, rank, world, local_rank, log):
                    "host_store_gib_per_rank": round(host_pages * page_bytes / 2**30, 2)},
         "exchange_bytes_per_layer": 4 * n * world,
         "stage_ms_per_step": {k: round(v, 3) for k, v in stage_ms.items()},
-        "timed": "CUDA graph replay of each step" if graph_ms is not None
-                 else "eager launches, NCCL all-gather per layer",
+        "timed": ("CUDA graphs, two per layer, the NCCL all-gather issued between them"
+                  if segmented else "CUDA graph replay of each step"),
         "eager_tok_s": round(steps / (eager_ms * 1e-3), 2),
         "stage_note": "one extra step, every stage timed alone; quest includes the all-gather",
         "per_rank": {"miss_rows_per_layer": round(misses / (steps * L), 1),

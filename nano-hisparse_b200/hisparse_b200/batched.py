@@ -116,7 +116,7 @@ class DecodeBatch:
 
     def layer(self, layer: int, query: torch.Tensor, out: torch.Tensor | None = None,
               counts: torch.Tensor | None = None, timing: list | None = None,
-              stages=None, serial: bool = False) -> torch.Tensor:
+              stages=None, serial: bool = False, part: str = "all") -> torch.Tensor:
         """Hot path of `layer` for query [B, Hq, D] (CUDA, contiguous) on the
         cache's compute stream; returns attention output [B, Hq, D].
 
@@ -128,18 +128,24 @@ class DecodeBatch:
         in `stages`). The events are external, so they also time graph replays
         when the call is captured. serial: run the ready-row attention after
         the gather instead of beside it (each stage then runs alone, for
-        per-stage timing)."""
-        cache, cfg, st, lib = self.cache, self.config, self.layers[layer], _lib.load()
-        if torch.cuda.current_stream(self.device) != self.compute:
+        per-stage timing).
+
+        part: "all" (default), or "head" / "tail" — the layer in two pieces
+        split at the exchange: "head" runs up to this rank's partial scores
+        (with a group) or the whole selection (without), "tail" everything
+        after, and neither runs the all-gather: the caller issues it between
+        them on the stream that orders the two (DecodeGraph's segmented
+        replay)."""
+        if part not in ("all", "head", "tail"):
+            raise ValueError("part must be 'all', 'head' or 'tail'")
+        cfg, st, compute = self.config, self.layers[layer], self.compute
+        if torch.cuda.current_stream(self.device) != compute:
             raise RuntimeError("DecodeBatch.layer must run on the batch's compute stream")
         b, hq, d = query.shape
         if b != self.batch or hq != self.q_heads or d != cfg.head_dim:
             raise ValueError("query must be [batch, q_heads, head_dim]")
         if out is None:
             out = torch.empty_like(query)
-        compute, transfer = self.compute, self.transfer
-        stream = compute.cuda_stream
-        status = self.status.data_ptr()
         if counts is None:
             counts = st.counts
         elif counts.shape != (b, 3) or counts.dtype != torch.int64 or not counts.is_contiguous():
@@ -152,6 +158,34 @@ class DecodeBatch:
             event.record(stream_)
             return event
 
+        t0 = None
+        if part != "tail":
+            t0 = self._select_head(layer, query, mark)
+        if part == "head":
+            return out
+        if part == "all":
+            self.exchange()
+        if self.group is not None:
+            self._select_tail(layer, query)
+        t1 = mark(compute, "quest", "resolve") if part == "all" else mark(compute, "resolve")
+        self._rest(layer, query, out, counts, timing, stages, serial, mark, t0, t1)
+        st.last_use = torch.cuda.Event()
+        st.last_use.record(compute)
+        return out
+
+    def exchange(self):
+        """All-gather of the partial scores over the group, on the current
+        stream (nothing without a group)."""
+        if self.group is not None:
+            import torch.distributed as dist
+
+            dist.all_gather_into_tensor(self.partials, self.partial, group=self.group)
+
+    def _select_head(self, layer, query, mark):
+        """The selection without a group; this rank's head sums with one."""
+        cfg, st, lib = self.config, self.layers[layer], _lib.load()
+        b, hq, d = query.shape
+        compute, stream, status = self.compute, self.compute.cuda_stream, self.status.data_ptr()
         if st.ready is not None:
             compute.wait_event(st.ready)
         t0 = mark(compute, "quest")
@@ -163,20 +197,30 @@ class DecodeBatch:
                 self.tokens.data_ptr(), self.width, self.token_counts.data_ptr(),
                 _lib.ptr(self.quest_ws), self.quest_ws_bytes, status, stream))
         else:
-            import torch.distributed as dist
-
-            # this rank's head sums, every rank's in shard order, the shared top-k
+            # this rank's head sums; the exchange and the shared top-k follow
             _lib.check(lib.hs_quest_partial_scores_batched(
                 b, query.data_ptr(), hq * d, _lib.dtype_code(query.dtype), st.min_ptrs.data_ptr(),
                 st.max_ptrs.data_ptr(), self._dtype, st.lengths.data_ptr(), hq, cfg.kv_heads, d,
                 self.max_pages, cfg.page_size, self.partial.data_ptr(), status, stream))
-            dist.all_gather_into_tensor(self.partials, self.partial, group=self.group)
-            _lib.check(lib.hs_quest_select_partials(
-                self.shards, self.partials.data_ptr(), b, st.lengths.data_ptr(), hq * self.shards,
-                self.max_pages, cfg.page_size, self.top_pages, int(self.keep_sink),
-                self.tokens.data_ptr(), self.width, self.token_counts.data_ptr(),
-                _lib.ptr(self.quest_ws), self.quest_ws_bytes, status, stream))
-        t1 = mark(compute, "quest", "resolve")
+        return t0
+
+    def _select_tail(self, layer, query):
+        """Every rank's head sums in shard order -> the shared top-k."""
+        cfg, st, lib = self.config, self.layers[layer], _lib.load()
+        b, hq = query.shape[0], query.shape[1]
+        _lib.check(lib.hs_quest_select_partials(
+            self.shards, self.partials.data_ptr(), b, st.lengths.data_ptr(), hq * self.shards,
+            self.max_pages, cfg.page_size, self.top_pages, int(self.keep_sink),
+            self.tokens.data_ptr(), self.width, self.token_counts.data_ptr(),
+            _lib.ptr(self.quest_ws), self.quest_ws_bytes, self.status.data_ptr(),
+            self.compute.cuda_stream))
+
+    def _rest(self, layer, query, out, counts, timing, stages, serial, mark, t0, t1):
+        """Resolve, gather, both attention phases and the merge of `layer`."""
+        cache, cfg, st, lib = self.cache, self.config, self.layers[layer], _lib.load()
+        b, hq, d = query.shape
+        compute, transfer = self.compute, self.transfer
+        stream, status = compute.cuda_stream, self.status.data_ptr()
         _lib.check(lib.hs_resolve_rows_batched(
             b, self.tokens.data_ptr(), self.width, st.src_ptrs.data_ptr(), st.res_ptrs.data_ptr(),
             st.table_pages, st.hot_ptrs.data_ptr(), cache.hot_blocks, st.tag_ptrs.data_ptr(),
@@ -228,9 +272,6 @@ class DecodeBatch:
                                 ("merge", t8, t9)):
                 if a is not None and b_ is not None:
                     timing.append((name, a, b_))
-        st.last_use = torch.cuda.Event()
-        st.last_use.record(compute)
-        return out
 
     def last_counts(self) -> torch.Tensor:
         """[layers, B, 3] resolver counts (resident hits, hot hits, misses) of
@@ -253,12 +294,24 @@ class DecodeGraph:
     previous step's readers of its hot rows.
     """
 
-    def __init__(self, batches, layers: int, timing=False):
+    def __init__(self, batches, layers: int, timing=False, segmented=None):
         """timing: False, True (every stage) or an iterable of stage names of
         DecodeBatch.layer; the captured step then records timing events, and
         after a replay ``self.timing`` holds that replay's (name, start, end)
-        pairs for every (layer, batch)."""
+        pairs for every (layer, batch).
+
+        segmented: capture each layer as two graphs split at the exchange
+        (DecodeBatch.layer's "head" and "tail") and issue the batches'
+        all-gathers between them at replay, so no collective is captured.
+        Default: when a batch has a process group (head-sharded selection).
+        A replay then costs the host two graph launches and one all-gather
+        per layer."""
         self.batches, self.layers = list(batches), layers
+        if segmented is None:
+            segmented = any(bt.group is not None for bt in self.batches)
+        self.segmented = bool(segmented)
+        if self.segmented and timing:
+            raise ValueError("a segmented step graph records no per-stage timing")
         for bt in self.batches:
             if bt.compute.cuda_stream == 0 or bt.transfer.cuda_stream == 0:
                 raise ValueError("DecodeGraph needs batches on created streams, not the default "
@@ -279,9 +332,23 @@ class DecodeGraph:
             self._run(None)
         torch.cuda.synchronize(self.device)
         self._reset_events()
-        self.graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(self.graph):
-            self._run(self.timing)
+        if self.segmented:
+            # thread-local capture: a process group's watchdog thread may query
+            # its collectives' events while a piece is being captured
+            self.graph, self.segments, pool = None, [], None
+            for layer in range(layers):
+                pair = []
+                for part in ("head", "tail"):
+                    graph = torch.cuda.CUDAGraph()
+                    with torch.cuda.graph(graph, pool=pool, capture_error_mode="thread_local"):
+                        self._run_part(layer, part)
+                    pool = graph.pool() if pool is None else pool
+                    pair.append(graph)
+                self.segments.append(tuple(pair))
+        else:
+            self.graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(self.graph):
+                self._run(self.timing)
         self._reset_events()
 
     def _reset_events(self):
@@ -305,5 +372,30 @@ class DecodeGraph:
             done.record(bt.compute)
             caller.wait_event(done)
 
+    def _run_part(self, layer, part):
+        """One piece of one layer for every batch, forked from and joined back
+        to the current (capturing) stream."""
+        caller = torch.cuda.current_stream(self.device)
+        start = torch.cuda.Event()
+        start.record(caller)
+        for bt in self.batches:
+            bt.compute.wait_event(start)
+        for i, bt in enumerate(self.batches):
+            with torch.cuda.stream(bt.compute):
+                bt.layer(layer, self.queries[i][layer], self.outputs[i][layer],
+                         self.counts[i][layer], part=part)
+        for bt in self.batches:
+            done = torch.cuda.Event()
+            done.record(bt.compute)
+            caller.wait_event(done)
+
     def replay(self):
-        self.graph.replay()
+        """One step on the current stream."""
+        if not self.segmented:
+            self.graph.replay()
+            return
+        for head, tail in self.segments:
+            head.replay()
+            for bt in self.batches:  # the same order on every rank
+                bt.exchange()
+            tail.replay()

@@ -213,8 +213,23 @@ def _batch_rank(rank, world, port, q, keys, length, p, top, out):
         with torch.cuda.stream(batch.compute):
             o = batch.layer(0, q[qs][None].to(dev).contiguous(), counts=counts)
         torch.cuda.synchronize(dev)
-        out[rank] = (batch.tokens[0].cpu().tolist(), counts.cpu().tolist(),
-                     bool(torch.isfinite(o).all()), lib_.device_flags(dev))
+        eager_tokens = batch.tokens[0].cpu().tolist()
+        # the same selection from a segmented step graph: the layer's two
+        # captured pieces with the all-gather issued between them at replay
+        from hisparse_b200.batched import DecodeGraph
+
+        streams = (torch.cuda.Stream(dev), torch.cuda.Stream(dev))
+        gbatch = DecodeBatch(cache, [0], 1, {0: mins}, {0: maxs}, top, q[qs].shape[0],
+                             group=dist.group.WORLD, streams=streams)
+        graph = DecodeGraph([gbatch], 1)
+        graph.queries[0][0].copy_(q[qs][None].to(dev))
+        graph.replay()
+        torch.cuda.synchronize(dev)
+        graph_result = (graph.segmented, gbatch.tokens[0].cpu().tolist(),
+                        bool(torch.isfinite(graph.outputs[0]).all()))
+        del graph
+        out[rank] = (eager_tokens, counts.cpu().tolist(), bool(torch.isfinite(o).all()),
+                     lib_.device_flags(dev), graph_result)
     finally:
         dist.destroy_process_group()
 
@@ -241,3 +256,5 @@ def test_head_sharded_decode_batch_on_two_ranks():
     assert [t for t in out[0][0] if t >= 0] == expected
     assert out[0][0] == out[1][0] and out[0][1] == out[1][1]
     assert out[0][2] and out[1][2] and not out[0][3] and not out[1][3]
+    for r in range(2):
+        assert out[r][4] == (True, out[r][0], True)
