@@ -57,6 +57,8 @@ def _metadata(gen, pages, hkv, d, dtype, spare=0):
     (6, 2, 24, 7, 1000, 9, torch.float16),
     (40, 8, 96, 5, 3001, 17, torch.float32),         # more than 32 query heads, C = 3
     (4, 4, 256, 3, 100, 2, torch.bfloat16),          # head_dim 256
+    (8, 2, 32, 16, 80000, 20, torch.float32),        # long table, register path (fp32)
+    (12, 4, 96, 16, 70001, 33, torch.float16),       # long table, register path (C = 3)
 ])
 def test_full_size_against_oracle(hq, hkv, d, p, length, top, dtype):
     gen = torch.Generator().manual_seed(hq * 1000 + length)
