@@ -122,10 +122,11 @@ HS_API int hs_host_device_pointer(const void *host, void **device_alias);
  * The head sums are combined the same way (lane j adds heads j, j+32, ...
  * left to right, then the same xor tree) and divided by q_heads.
  */
-/* Workspace: per-request scores plus one completion counter per request. It
- * must be zero-filled before its first use; every call leaves it zero-filled,
- * so one workspace serves consecutive calls on one stream (calls that overlap
- * on the GPU need separate workspaces). */
+/* Workspace: per-request scores plus one completion counter per request. The
+ * counters must be zero before the first use (zero-fill the whole workspace
+ * once); every call overwrites the scores and leaves the counters zero, so
+ * one workspace serves consecutive calls on one stream (calls that overlap on
+ * the GPU need separate workspaces). */
 HS_API size_t hs_quest_workspace_bytes(int batch, int64_t max_pages);
 
 HS_API int hs_quest_select(const void *query, int query_dtype, const void *minimum,
