@@ -164,3 +164,44 @@ def test_oracle_append_matches_reference_fixtures(golden):
                 assert np.array_equal(summ, c["summary_after"].numpy()), case["name"]
                 chunks += 1
     assert chunks > 60
+
+
+def test_oracle_select_ranking_rule():
+    """The oracle's ranking, which every selection kernel matches token for
+    token, is the rule the header states: forced tail (and sink) pages, then
+    the highest scores with -0 equal to +0, NaN above +inf and equal scores
+    taking the lower page; checked against a plain sort on random scores with
+    ties, signed zeros, infinities and NaN."""
+    rng = np.random.default_rng(3)
+    for trial in range(400):
+        n = int(rng.integers(2, 400))
+        top = int(rng.integers(1, n + 3))
+        p = int(rng.integers(1, 9))
+        length = (n - 1) * p + int(rng.integers(1, p + 1))
+        kind = trial % 4
+        if kind == 0:
+            s = rng.normal(200, 20, n)
+        elif kind == 1:
+            s = rng.integers(0, 3, n).astype(float)
+        elif kind == 2:
+            s = rng.choice([0.0, -0.0, 1.0, -1.0], n)
+        else:
+            s = rng.normal(0, 1e3, n)
+            s[rng.integers(0, n, 4)] = np.nan
+            s[rng.integers(0, n, 3)] = np.inf
+            s[rng.integers(0, n, 3)] = -np.inf
+        s = s.astype(np.float32)
+        sink = bool(rng.integers(0, 2))
+        tokens, count = oracle.quest_select(s, length, p, top, sink, max(top * p, length))
+        if top >= n:
+            pages = list(range(n))
+        else:
+            def rank(page):
+                if page == n - 1 or (sink and top > 1 and page == 0):
+                    return (0, 0.0, page)
+                v = float(s[page])
+                return (1, 0.0, page) if np.isnan(v) else (2, -(v + 0.0), page)
+            pages = sorted(sorted(range(n), key=rank)[:top])
+        want = [t for pg in pages for t in range(pg * p, min(pg * p + p, length))]
+        assert tokens[:count].tolist() == want, (trial, n, top, sink)
+        assert set(tokens[count:].tolist()) <= {-1}
