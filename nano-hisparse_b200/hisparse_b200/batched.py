@@ -102,7 +102,14 @@ class DecodeBatch:
         if group is not None:
             import torch.distributed as dist
 
+            from .sharded import same_on_every_rank
+
             self.shards = dist.get_world_size(group)
+            # the per-layer all-gather exchanges [batch * max_pages] partials:
+            # every rank must hold the same shape
+            if not same_on_every_rank(group, (b, self.max_pages, top_pages), dev):
+                raise ValueError("ranks disagree on the batch size, the metadata table "
+                                 "length or the page budget of a head-sharded batch")
             self.partial = torch.empty(b * self.max_pages, dtype=torch.float32, device=dev)
             self.partials = torch.empty((self.shards, b * self.max_pages), dtype=torch.float32,
                                         device=dev)

@@ -41,31 +41,77 @@ def head_slice(kv_heads: int, q_heads: int, rank: int, world: int) -> tuple[slic
     return slice(rank * kl, (rank + 1) * kl), slice(rank * ql, (rank + 1) * ql)
 
 
+def group_world(group) -> int:
+    """Ranks that share one selection: the size of `group`, or 1 when no group
+    is given. A process group that merely exists (e.g. a request-sharded job
+    that initialised torch.distributed for its reporting) never joins an
+    exchange implicitly: the caller names the group its heads are split over."""
+    if group is None:
+        return 1
+    import torch.distributed as dist
+
+    return dist.get_world_size(group)
+
+
+def same_on_every_rank(group, values, device=None) -> bool:
+    """True when every rank of `group` passed the same integers. One small
+    all-reduce (MAX of each value and of its negation) on the group's backend;
+    every rank gets the same answer, so all raise or none does."""
+    import torch.distributed as dist
+
+    t = torch.tensor([int(v) for v in values] + [-int(v) for v in values], dtype=torch.int64)
+    if dist.get_backend(group) == "nccl":
+        t = t.to(device if device is not None else torch.device("cuda",
+                                                                torch.cuda.current_device()))
+    dist.all_reduce(t, op=dist.ReduceOp.MAX, group=group)
+    t, k = t.cpu(), len(values)
+    return all(int(t[i]) == -int(t[k + i]) for i in range(k))
+
+
+def _argument_problem(query, minimum, maximum, count, top_pages):
+    """The ValueError message quest_selection would raise, or None."""
+    if top_pages < 1 or query.shape[0] % minimum.shape[1]:
+        return "invalid page budget or GQA shape"
+    if top_pages >= count:
+        return None
+    if minimum.shape != maximum.shape or minimum.dtype != maximum.dtype:
+        return "minimum and maximum metadata must match"
+    if minimum.ndim != 3 or query.ndim != 2 or minimum.shape[2] != query.shape[1]:
+        return "expected query [heads, dim] and metadata [pages, kv_heads, dim]"
+    if minimum.shape[0] < count:
+        return "metadata has fewer pages than the selection length"
+    return None
+
+
 def sharded_quest_selection(query, minimum, maximum, length, page_size, top_pages,
                             keep_sink=True, group=None):
     """quest_selection over heads split across the ranks of `group`.
 
     query [Hq_local, D], minimum/maximum [>= pages, Hkv_local, D]: this rank's
     slices (see head_slice). Returns the device-form Selection, identical on
-    every rank, with `heads` = the query heads of all ranks.
+    every rank, with `heads` = the query heads of all ranks. Without a group
+    the selection is this rank's alone (no collective). Every rank must pass
+    the same length, page size, budget and metadata table length: these are
+    compared across the group first (the all-gather needs equal sizes on every
+    rank), and a mismatch raises ValueError on every rank.
     """
     import torch.distributed as dist
 
-    world = dist.get_world_size(group) if group is not None or (
-        dist.is_available() and dist.is_initialized()) else 1
+    world = group_world(group)
     count = ceil(length / page_size)
     heads = query.shape[0] * world
-    if top_pages < 1 or query.shape[0] % minimum.shape[1]:
-        raise ValueError("invalid page budget or GQA shape")
+    problem = _argument_problem(query, minimum, maximum, count, top_pages)
+    if world > 1 and not same_on_every_rank(
+            group, (minimum.shape[0], length, page_size, top_pages, bool(keep_sink),
+                    problem is None), query.device):
+        # compared before any rank can branch, so no rank waits alone in the exchange
+        raise ValueError("ranks disagree on the metadata table length, the selection "
+                         "length, the page size, the page budget or argument validity")
+    if problem is not None:
+        raise ValueError(problem)
     if top_pages >= count:
         return Selection.from_pages(list(range(count)), length, page_size, heads, "quest")
     _lib.require_cuda(query, minimum, maximum)
-    if minimum.shape != maximum.shape or minimum.dtype != maximum.dtype:
-        raise ValueError("minimum and maximum metadata must match")
-    if minimum.ndim != 3 or query.ndim != 2 or minimum.shape[2] != query.shape[1]:
-        raise ValueError("expected query [heads, dim] and metadata [pages, kv_heads, dim]")
-    if minimum.shape[0] < count:
-        raise ValueError("metadata has fewer pages than the selection length")
     lib = _lib.load()
     device = query.device
     query, minimum, maximum = query.contiguous(), minimum.contiguous(), maximum.contiguous()

@@ -86,3 +86,38 @@ def test_two_ranks_exchange_partial_scores_in_rank_order():
     mp.start_processes(_sharded_worker, args=(world, _free_port(), out), nprocs=world,
                        start_method="spawn", join=True)
     assert out[0] == out[1] and len(out[0]) == world and out[0][0] != out[0][1]
+
+
+def _agreement_worker(rank, world, port, out):
+    import sys
+    from pathlib import Path
+
+    root = Path(__file__).resolve().parent.parent
+    sys.path.insert(0, str(root / "nano-hisparse_b200"))
+    from hisparse_b200.sharded import group_world, same_on_every_rank
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        group = dist.group.WORLD
+        out[rank] = (
+            group_world(None),                                  # no group: this rank alone
+            group_world(group),
+            same_on_every_rank(group, (2048, 32768, 16, 128)),  # equal on both ranks
+            same_on_every_rank(group, (2048 + rank, 32768)),    # table lengths differ
+            same_on_every_rank(group, (7, -3 * rank)),          # one negative value differs
+        )
+    finally:
+        dist.destroy_process_group()
+
+
+def test_head_sharded_exchange_checks_agreement_and_needs_a_named_group():
+    """An initialised default group does not make a selection head-sharded
+    (group=None is one rank), and ranks whose exchange sizes differ are caught
+    on every rank before the all-gather."""
+    world = 2
+    manager = mp.get_context("spawn").Manager()
+    out = manager.dict()
+    mp.start_processes(_agreement_worker, args=(world, _free_port(), out), nprocs=world,
+                       start_method="spawn", join=True)
+    assert out[0] == out[1] == (1, 2, True, False, False)
