@@ -24,6 +24,12 @@ weights_only=True):
                       test_trace.py), with the final row counters
   append_cases.pt     every HostStore.append (storage.py:296-321) of scripted
                       prefill + decode sessions, with the state before/after
+  quest_full_cases.pt quest_selection at the full sizes the bench runs
+                      (configuration 2: 2,048-2,050 pages; configuration 3:
+                      8,192 / 2,048 pages; configuration 5: 16,389 pages), on
+                      inputs regenerated from a seed by
+                      tests/helpers.full_quest_inputs; each case records the
+                      seed, the inputs' sha256 and the reference's pages
 """
 
 from __future__ import annotations
@@ -201,6 +207,40 @@ def quest_cases(ref):
             case[f"tokens_{int(sink)}"] = list(sel.positions[0])
             case[f"pages_{int(sink)}"] = sel.pages
         cases.append(case)
+    return cases
+
+
+# full-size cases: (name, Hq, Hkv, D, page, length, top pages, seeds)
+FULL_QUEST = [
+    ("config2", 32, 8, 128, 16, [32768, 32769, 32800, 32768, 32769, 32800], 128,
+     [11, 12, 13, 14, 15, 16]),
+    ("config3_p16", 32, 8, 128, 16, [131072, 131072], 256, [31, 32]),
+    ("config3_p64", 32, 8, 128, 64, [131072, 131072], 64, [33, 34]),
+    ("config5", 28, 4, 128, 64, [1048833, 1048833, 1048833], 128, [51, 52, 53]),
+]
+FULL_SPARE_PAGES = 16  # table capacity beyond the selection length, as in a live cache
+
+
+def quest_full_cases(ref):
+    from nano_hisparse.selection import quest_selection
+
+    sys.path.insert(0, str(OUT.parent))
+    from helpers import full_quest_inputs
+
+    cases = []
+    for name, hq, hkv, d, p, lengths, top, seeds in FULL_QUEST:
+        for length, seed in zip(lengths, seeds):
+            pages = math.ceil(length / p)
+            q, mn, mx, digest = full_quest_inputs(hq, hkv, d, p, pages + FULL_SPARE_PAGES, seed)
+            case = {"name": f"{name}_seed{seed}", "q_heads": hq, "kv_heads": hkv,
+                    "head_dim": d, "page_size": p, "length": length,
+                    "max_pages": pages + FULL_SPARE_PAGES, "top_pages": top, "seed": seed,
+                    "dtype": "bfloat16", "digest": digest}
+            for sink in (True, False):
+                sel = quest_selection(q, mn, mx, length, p, top, keep_sink=sink)
+                case[f"pages_{int(sink)}"] = sel.pages
+            cases.append(case)
+            print(f"  {case['name']}: {pages} pages", flush=True)
     return cases
 
 
@@ -571,7 +611,7 @@ def main():
     torch.set_num_threads(4)
     for name, fn in [("resolver_cases", resolver_cases), ("quest_cases", quest_cases),
                      ("attention_cases", attention_cases), ("scenarios", scenarios),
-                     ("append_cases", append_cases)]:
+                     ("append_cases", append_cases), ("quest_full_cases", quest_full_cases)]:
         if args.only and name not in args.only:
             continue
         data = fn(ref)

@@ -17,6 +17,40 @@ TOL = {
 }
 
 
+def full_quest_inputs(q_heads, kv_heads, head_dim, page_size, pages, seed,
+                      dtype=torch.bfloat16, chunk=1024):
+    """Seeded Quest inputs at full configuration sizes, regenerated wherever a
+    test needs them (the metadata of one configuration-5 layer is 33 MB, too
+    large to commit): q ~ N(0,1) [q_heads, head_dim]; K ~ N(0,1) drawn page
+    chunk by page chunk as [chunk, page_size, kv_heads, head_dim]; the page
+    bounds are K's min/max over each page's tokens, in `dtype`.
+    Returns (q, minimum, maximum, digest), digest = sha256 of their bytes,
+    which a fixture records so a changed generator is caught, not mistaken
+    for a parity failure."""
+    import hashlib
+
+    gen = torch.Generator().manual_seed(seed)
+    q = torch.randn(q_heads, head_dim, generator=gen).to(dtype)
+    mn = torch.empty((pages, kv_heads, head_dim), dtype=dtype)
+    mx = torch.empty_like(mn)
+    for lo in range(0, pages, chunk):
+        n = min(chunk, pages - lo)
+        keys = torch.randn(n, page_size, kv_heads, head_dim, generator=gen).to(dtype)
+        mn[lo:lo + n] = keys.amin(1)
+        mx[lo:lo + n] = keys.amax(1)
+    h = hashlib.sha256()
+    for t in (q, mn, mx):
+        h.update(raw_numpy(t).tobytes())
+    return q, mn, mx, h.hexdigest()
+
+
+def pages_to_tokens(pages, length, page_size):
+    """Selection.from_pages' expansion: every token of the pages in ascending
+    order, the last page clipped at `length`."""
+    return [t for p in sorted(pages)
+            for t in range(p * page_size, min((p + 1) * page_size, length))]
+
+
 def raw_numpy(t: torch.Tensor) -> np.ndarray:
     """Byte-exact numpy copy of a CPU tensor (16-bit floats as uint16)."""
     t = t.detach().cpu().contiguous()
@@ -66,26 +100,24 @@ def forced_pages(pages, top_pages, keep_sink):
     return forced
 
 
-def quest_sets_agree(expected_tokens, got_tokens, query, minimum, maximum, length, page_size,
-                     top_pages, keep_sink, rel=1e-5):
-    """Selections agree exactly, or differ only in pages whose exact (fp64)
-    scores tie with the k-th score to within `rel` (fp32 summation order is
-    left unspecified by the reference). Returns (ok, detail)."""
-    if list(expected_tokens) == list(got_tokens):
-        return True, "identical"
+def near_tie_report(expected_tokens, got_tokens, query, minimum, maximum, length,
+                    page_size, top_pages, keep_sink):
+    """Explains a selection that differs from the reference's: the pages in
+    which they differ, each with its exact (fp64) score and its relative gap
+    to the k-th chosen score. Selections must be identical; this only names
+    what differs, for the failure message."""
     pages = math.ceil(length / page_size)
     a = {t // page_size for t in expected_tokens}
     b = {t // page_size for t in got_tokens}
     if len(a) != len(b):
-        return False, f"page counts differ: {len(a)} vs {len(b)}"
+        return f"page counts differ: {len(a)} vs {len(b)}"
     scores = quest_scores_fp64(query, minimum, maximum, pages)
     forced = forced_pages(pages, top_pages, keep_sink)
     chosen = sorted((p for p in a if p not in forced), key=lambda p: scores[p])
     if not chosen:
-        return False, "forced pages differ"
+        return "forced pages differ"
     kth = scores[chosen[0]]
-    scale = max(abs(kth), np.abs(scores).max() * 1e-3, 1e-30)
-    for p in a ^ b:
-        if p in forced or abs(scores[p] - kth) > rel * scale:
-            return False, f"page {p} score {scores[p]!r} vs k-th {kth!r}"
-    return True, f"near-tie pages {sorted(a ^ b)}"
+    return ", ".join(f"page {p}: fp64 score {scores[p]!r}, gap to k-th "
+                     f"{(scores[p] - kth) / max(abs(kth), 1e-30):+.3e} (relative)"
+                     + (" [forced]" if p in forced else "")
+                     for p in sorted(a ^ b))

@@ -7,7 +7,7 @@ import pytest
 import torch
 
 import oracle
-from helpers import quest_sets_agree
+from helpers import full_quest_inputs, near_tie_report, pages_to_tokens
 from hisparse_b200 import LogicalTopK, Selection, _lib, quest_selection
 from hisparse_b200.selection import quest_selection as qs
 
@@ -20,7 +20,7 @@ def _tokens(sel):
 
 
 def test_reference_fixtures(golden):
-    identical = 0
+    checked = 0
     for case in golden("quest_cases"):
         q, mn, mx = (case[k].to(DEV) for k in ("query", "minimum", "maximum"))
         for sink in (0, 1):
@@ -34,12 +34,64 @@ def test_reference_fixtures(golden):
             assert got == oracle.quest_tokens(case["query"], case["minimum"], case["maximum"],
                                               case["length"], case["page_size"],
                                               case["top_pages"], bool(sink)), case["name"]
-            ok, detail = quest_sets_agree(case[key], got, case["query"], case["minimum"],
-                                          case["maximum"], case["length"], case["page_size"],
-                                          case["top_pages"], bool(sink))
-            assert ok, f"{case['name']}: {detail}"
-            identical += detail == "identical"
-    assert identical >= 50
+            # and token for token the reference's selection
+            assert got == list(case[key]), f"{case['name']} sink={sink}: " + near_tie_report(
+                case[key], got, case["query"], case["minimum"], case["maximum"],
+                case["length"], case["page_size"], case["top_pages"], bool(sink))
+            checked += 1
+    assert checked == 62
+    assert not _lib.device_flags(DEV)
+
+
+def _full_cases(golden):
+    """Full-size reference cases grouped by shape, inputs regenerated from
+    their seeds (digest-checked)."""
+    groups = {}
+    for case in golden("quest_full_cases"):
+        q, mn, mx, digest = full_quest_inputs(case["q_heads"], case["kv_heads"],
+                                              case["head_dim"], case["page_size"],
+                                              case["max_pages"], case["seed"])
+        assert digest == case["digest"], f"{case['name']}: input generator changed"
+        key = (case["q_heads"], case["kv_heads"], case["head_dim"], case["page_size"],
+               case["max_pages"], case["top_pages"])
+        groups.setdefault(key, []).append((case, q, mn, mx))
+    return groups
+
+
+def test_full_size_selections_equal_the_reference(golden):
+    """The kernels' selections at the sizes the bench runs equal the
+    reference's, page for page: the single-request entry point and the
+    batched one (all seeds of a shape in one launch; configuration 5's 16,389
+    pages take the partial-score + cluster-select path), sink on and off."""
+    lib = _lib.load()
+    stream = torch.cuda.current_stream().cuda_stream
+    for (hq, hkv, d, p, max_pages, top), cases in _full_cases(golden).items():
+        dq = torch.stack([q for _, q, _, _ in cases]).to(DEV)
+        dmins = [mn.to(DEV) for _, _, mn, _ in cases]
+        dmaxs = [mx.to(DEV) for _, _, _, mx in cases]
+        b, width = len(cases), top * p
+        mptr = torch.tensor([t.data_ptr() for t in dmins], dtype=torch.int64, device=DEV)
+        xptr = torch.tensor([t.data_ptr() for t in dmaxs], dtype=torch.int64, device=DEV)
+        lens = torch.tensor([c["length"] for c, *_ in cases], dtype=torch.int32, device=DEV)
+        tokens = torch.empty(b, width, dtype=torch.int32, device=DEV)
+        counts = torch.empty(b, dtype=torch.int32, device=DEV)
+        nbytes = lib.hs_quest_workspace_bytes(b, max_pages)
+        ws = torch.zeros(nbytes, dtype=torch.uint8, device=DEV)
+        for sink in (1, 0):
+            _lib.check(lib.hs_quest_select_batched(
+                b, dq.data_ptr(), hq * d, _lib.HS_BFLOAT16, mptr.data_ptr(), xptr.data_ptr(),
+                _lib.HS_BFLOAT16, lens.data_ptr(), hq, hkv, d, max_pages, p, top, sink,
+                tokens.data_ptr(), width, counts.data_ptr(), ws.data_ptr(), nbytes, 0, stream))
+            batched = tokens.cpu().tolist()
+            for i, (case, q, mn, mx) in enumerate(cases):
+                want = pages_to_tokens(case[f"pages_{sink}"], case["length"], p)
+                single = _tokens(quest_selection(dq[i], dmins[i], dmaxs[i], case["length"], p,
+                                                 top, keep_sink=bool(sink)))
+                for form, got in (("single", single),
+                                  ("batched", batched[i][:int(counts[i])])):
+                    assert got == want, f"{case['name']} sink={sink} {form}: " + \
+                        near_tie_report(want, got, q, mn, mx, case["length"], p, top,
+                                        bool(sink))
     assert not _lib.device_flags(DEV)
 
 

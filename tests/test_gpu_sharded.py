@@ -11,7 +11,7 @@ import pytest
 import torch
 
 import oracle
-from helpers import quest_sets_agree
+from helpers import full_quest_inputs, near_tie_report, pages_to_tokens
 from hisparse_b200 import _lib, quest_selection
 from hisparse_b200.sharded import head_slice, sharded_quest_selection
 
@@ -97,8 +97,8 @@ def test_emulated_shards_match_oracle(shards, hq, hkv, d, p, length, top, dtype)
 
 
 def test_sharded_selection_agrees_with_reference(golden):
-    """The reference averages over all heads in torch's order; the sharded sum
-    may differ from it only at near-ties of the k-th score."""
+    """The reference averages over all heads in torch's order; the sharded
+    fixed-order sum picks the same pages on every recorded case."""
     checked = 0
     for case in golden("quest_cases"):
         hq, hkv = case["query"].shape[0], case["minimum"].shape[1]
@@ -110,12 +110,36 @@ def test_sharded_selection_agrees_with_reference(golden):
         pages = math.ceil(case["length"] / case["page_size"])
         if case["top_pages"] >= pages:
             continue
-        ok, detail = quest_sets_agree(case["tokens_1"], got, case["query"], case["minimum"],
-                                      case["maximum"], case["length"], case["page_size"],
-                                      case["top_pages"], True)
-        assert ok, f"{case['name']}: {detail}"
+        assert list(got) == list(case["tokens_1"]), f"{case['name']}: " + near_tie_report(
+            case["tokens_1"], got, case["query"], case["minimum"], case["maximum"],
+            case["length"], case["page_size"], case["top_pages"], True)
         checked += 1
     assert checked >= 5
+
+
+@pytest.mark.parametrize("shards", [2, 4])
+def test_sharded_full_size_equals_reference(golden, shards):
+    """Configuration 5 at full size (16,389 pages, 28 / 4 heads split over 2 or
+    4 shards): the shard-ordered selection equals the reference's recorded
+    selection page for page, sink on and off."""
+    checked = 0
+    for case in golden("quest_full_cases"):
+        if not case["name"].startswith("config5"):
+            continue
+        q, mn, mx, digest = full_quest_inputs(case["q_heads"], case["kv_heads"],
+                                              case["head_dim"], case["page_size"],
+                                              case["max_pages"], case["seed"])
+        assert digest == case["digest"], f"{case['name']}: input generator changed"
+        p, top, length = case["page_size"], case["top_pages"], case["length"]
+        for sink in (1, 0):
+            got, _ = _emulated(q.to(DEV), mn.to(DEV), mx.to(DEV), length, p, top, bool(sink),
+                               shards)
+            want = pages_to_tokens(case[f"pages_{sink}"], length, p)
+            assert got == want, f"{case['name']} sink={sink} shards={shards}: " + \
+                near_tie_report(want, got, q, mn, mx, length, p, top, bool(sink))
+            checked += 1
+    assert checked == 6
+    assert not _lib.device_flags(DEV)
 
 
 def _free_port():
