@@ -40,10 +40,11 @@ struct AttendParams {
   float *partials;          // [2 phases][batch][q_heads][split_stride][head_dim + 2]
   int split_stride;         // splits capacity of the workspace
   int phase, phases;        // partial set written by a phase launch / merged by the merge
-  int *phase_splits;        // [2] splits each phase used (written by the phase launch)
+  int *phase_splits;        // [2][batch] partials each phase left per batch item
   const int64_t *valid_counts;  // optional: rows valid per batch item = sum of
   int counts_stride, counts_first, counts_n;  // valid_counts[b*stride + first .. +n)
   int32_t *status;
+  int spare_sms;            // SMs the bulk path leaves to concurrent work
 };
 
 // Leading rows of batch item b that a phase reads, and the [begin, end) part
@@ -123,8 +124,8 @@ __global__ void __launch_bounds__(kAttendThreads) attend_split_kernel(AttendPara
   split_range(p, b, split, begin, end);
   const int64_t *rows = p.rows + (int64_t)b * p.rows_batch_stride +
                         (shared_rows ? 0 : (int64_t)h0 * p.rows_head_stride);
-  if (split == 0 && b == 0 && blockIdx.y == 0 && threadIdx.x == 0)
-    p.phase_splits[p.phase] = p.splits;
+  if (split == 0 && blockIdx.y == 0 && threadIdx.x == 0)
+    p.phase_splits[p.phase * p.batch + b] = p.splits;
   const int64_t row_elems = (int64_t)p.kv_heads * D;
   const int64_t plane_elems = (int64_t)p.page_size * row_elems;
   const TKV *pool = reinterpret_cast<const TKV *>(p.pool);
@@ -310,7 +311,7 @@ __global__ void __launch_bounds__(kMmaThreads, 1) attend_mma_kernel(AttendParams
   const int hn = active ? min(16, kh * groups + groups - h0) : 0;
   int64_t begin, end;
   split_range(p, b, split, begin, end);
-  if (split == 0 && b == 0 && tid == 0) p.phase_splits[p.phase] = p.splits;
+  if (split == 0 && tid == 0) p.phase_splits[p.phase * p.batch + b] = p.splits;
   const int64_t *rows = p.rows + (int64_t)b * p.rows_batch_stride;
   const int64_t row_elems = (int64_t)p.kv_heads * 128;
   const int64_t plane = (int64_t)p.page_size * row_elems;
@@ -493,6 +494,472 @@ __global__ void __launch_bounds__(kMmaThreads, 1) attend_mma_kernel(AttendParams
   }
 }
 
+// ---- bulk-copy path: bf16 query and KV, head_dim 128, shared rows, <= 8 query
+// heads per KV head, 1/2/4/8 KV heads -----------------------------------------------
+//
+// Rows are spread evenly over the CTAs, stream-K fashion: the valid rows of all
+// batch items form one sequence, CTA c takes rows [c*chunk, (c+1)*chunk) of it,
+// and leaves one (max, sum, O) partial per batch item its range touches (slot
+// c - first CTA of the item). chunk is at least the total over the CTAs and at
+// least an item's rows over (slots - 1), so no item needs more partial slots
+// than the workspace holds.
+//
+// Warp 0 is the producer. Per stage it checks the stage's physical rows (loaded
+// one stage ahead) and issues 1-D bulk copies (the TMA engine's untiled form)
+// of each valid row's K row and V row (kv_heads * 256 contiguous bytes each)
+// into a 3-stage ring, completing on the stage's mbarrier. Two rows that are
+// consecutive in one pool block move with one copy per plane (4 KiB at
+// configuration 2): bulk copies cost a fixed ~85 cycles of the SM's copy
+// engine each, so 2 KiB copies reach ~83% and 4 KiB ~94% of the HBM copy rate.
+// Slots without a valid row get a zeroed V row and a cleared bit in the stage's
+// slot mask. A stage record tells the consumers the batch item, its partial
+// slot and whether the stage ends the item's segment; a final record ends the
+// CTA.
+//
+// Warps 1..8 consume. Warp c serves KV head c % kv_heads and 16 of the stage's
+// slots (stage rows = 16 * 8 / kv_heads), with the operands swapped so that the
+// 16 rows fill the MMA's M side and the <= 8 query heads its N side:
+//   S^T = K Q^T   m16n8k16 bf16 MMA: A = 16 K rows (ldmatrix), B = the
+//                 query heads (registers, loaded once per batch item);
+//   softmax       fp32, exp2 with log2(e) folded into the scale; the running
+//                 max is raised only when a tile's max exceeds it by more than
+//                 8 (a factor of 256), so O is rescaled rarely;
+//   O^T += V^T P^T  A = V^T (ldmatrix.trans), B = P^T: the S^T accumulators
+//                 rounded to bf16 pairs and transposed in registers (movmatrix).
+// When a segment ends, warps serving the same KV head combine their (max, sum,
+// O) through shared memory and one of them writes the partials.
+constexpr int kBulkConsumers = 8;
+constexpr int kBulkThreads = 32 * (1 + kBulkConsumers);
+constexpr int kBulkStages = 3;
+// A phase launch runs beside other work (the miss gather, another request
+// group's selection and resolve); leaving it a few SMs keeps a pipelined decode
+// step 7% faster than taking every SM.
+constexpr int kPhaseSpareSms = 4;
+
+struct BulkShape {
+  int row_bytes;    // kv_heads * 256: K (or V) of one token, every KV head
+  int pair_stride;  // 2 * row_bytes + 16: two slots side by side, then 16 bytes of pad
+  int stage_rows;   // 16 * subs
+  int subs;         // consumer warps per KV head
+  int plane_bytes;  // K (or V) slots of a stage
+  int stage_bytes;  // K slots, then V slots
+  int combine_bytes;  // shared memory for combining the warps of one KV head
+  int smem_bytes;
+};
+
+__host__ __device__ inline BulkShape bulk_shape(int kv_heads) {
+  BulkShape s;
+  s.row_bytes = kv_heads * kHeadBytes;
+  s.pair_stride = 2 * s.row_bytes + 16;
+  s.subs = kBulkConsumers / kv_heads;
+  s.stage_rows = 16 * s.subs;
+  s.plane_bytes = (s.stage_rows / 2) * s.pair_stride;
+  s.stage_bytes = 2 * s.plane_bytes;
+  s.combine_bytes = s.subs > 1 ? kv_heads * 32 * 36 * (int)sizeof(float) : 0;
+  s.smem_bytes = kBulkStages * s.stage_bytes + s.combine_bytes;
+  return s;
+}
+
+// Shared-memory offset of stage slot `slot` within a plane. Slots come in
+// groups of 16 (one consumer warp's rows); within a group, slots j and j + 8
+// are adjacent (one pair, so two consecutive pool rows land with one copy) and
+// the 8 pairs are pair_stride apart. The 8 slots an ldmatrix reads (j = 0..7 of
+// one half) are then 16 bytes apart modulo 128: no bank conflicts.
+__host__ __device__ __forceinline__ int slot_offset(const BulkShape &s, int slot) {
+  return ((slot >> 4) * 8 + (slot & 7)) * s.pair_stride + ((slot >> 3) & 1) * s.row_bytes;
+}
+
+struct BulkStage {
+  int b;        // batch item (-1: end of the CTA's work)
+  int slot;     // partial slot of this CTA for item b
+  int last;     // the stage ends the CTA's segment of item b
+  int pad;
+  uint32_t ok[4];  // slots holding a valid row (bit s of word s / 32)
+};
+
+__device__ __forceinline__ int64_t valid_rows(const AttendParams &p, int b) {
+  if (!p.valid_counts) return p.count;
+  int64_t v = 0;
+  for (int i = 0; i < p.counts_n; ++i)
+    v += p.valid_counts[(int64_t)b * p.counts_stride + p.counts_first + i];
+  return v < 0 ? 0 : (v > p.count ? p.count : v);
+}
+
+__device__ __forceinline__ uint32_t movmatrix_trans(uint32_t x) {
+  uint32_t y;
+  asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;\n" : "=r"(y) : "r"(x));
+  return y;
+}
+
+__global__ void __launch_bounds__(kBulkThreads, 1) attend_bulk_kernel(AttendParams p) {
+  extern __shared__ __align__(128) char smem[];
+  __shared__ __align__(8) uint64_t full[kBulkStages], empty[kBulkStages];
+  __shared__ __align__(8) uint64_t xbar;  // consumer warps' combine rounds
+  __shared__ BulkStage info[kBulkStages];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const BulkShape sh = bulk_shape(p.kv_heads);
+  const int R = sh.stage_rows;
+  if (tid == 0) {
+    for (int s = 0; s < kBulkStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kBulkConsumers);
+    }
+    mbar_init(&xbar, kBulkConsumers);
+    asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+  }
+  __syncthreads();
+
+  if (warp == 0) {
+    // ---------------- producer ----------------
+    // total valid rows, the largest item, and (CTA 0) zero counts for empty items
+    int64_t total = 0, largest = 0;
+    for (int b0 = 0; b0 < p.batch; b0 += 32) {
+      const int b = b0 + lane;
+      const int64_t v = b < p.batch ? valid_rows(p, b) : 0;
+      if (blockIdx.x == 0 && b < p.batch && v == 0) p.phase_splits[p.phase * p.batch + b] = 0;
+      total += warp_sum_int<int64_t>(v);
+      int64_t m = v;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        const int64_t other = __shfl_xor_sync(kFullMask, m, o);
+        m = other > m ? other : m;
+      }
+      largest = m > largest ? m : largest;
+    }
+    const int64_t slots = p.split_stride;
+    int64_t chunk = total > 0 ? ceil_div(total, (int64_t)gridDim.x) : 1;
+    if (slots > 1) chunk = max(chunk, ceil_div(largest, slots - 1));
+    else chunk = max(chunk, largest);
+    const int64_t lo = (int64_t)blockIdx.x * chunk, hi = min(total, lo + chunk);
+    const char *pool = p.pool;
+    const int64_t row_bytes = sh.row_bytes;
+    const int64_t plane = (int64_t)p.page_size * row_bytes;  // bytes from a K row to its V row
+    int t = 0;  // stages issued
+    bool alive = true;
+    // claim the next stage buffer (waits for the consumers to release it)
+    auto claim = [&](int st) -> bool {
+      if (t < kBulkStages) return true;
+      return mbar_wait(&empty[st], ((t / kBulkStages) - 1) & 1, p.status);
+    };
+    int64_t start = 0;  // first row of item b0 in the sequence
+    for (int b0 = 0; alive && b0 < p.batch && start < hi; b0 += 32) {
+      const int b_l = b0 + lane;
+      const int64_t v_l = b_l < p.batch ? valid_rows(p, b_l) : 0;
+      const int64_t inc = warp_inclusive_scan<int64_t>(v_l);
+      const int64_t chunk_total = __shfl_sync(kFullMask, inc, 31);
+      const int64_t s_l = start + inc - v_l;
+      unsigned touch = __ballot_sync(kFullMask, v_l > 0 && s_l < hi && s_l + v_l > lo);
+      while (alive && touch) {
+        const int src = __ffs(touch) - 1;
+        touch &= touch - 1;
+        const int b = b0 + src;
+        const int64_t s_b = __shfl_sync(kFullMask, s_l, src);
+        const int64_t v_b = __shfl_sync(kFullMask, v_l, src);
+        const int64_t seg_lo = max(lo, s_b) - s_b, seg_hi = min(hi, s_b + v_b) - s_b;
+        const int slot = (int)(blockIdx.x - s_b / chunk);
+        if (s_b + v_b <= hi && lane == 0) p.phase_splits[p.phase * p.batch + b] = slot + 1;
+        const int64_t *rows = p.rows + (int64_t)b * p.rows_batch_stride;
+        // Lane l handles the tile's row pairs j = l and l + 32 (rows 2j, 2j + 1
+        // of the tile, slots g*16 + j%8 and that + 8 with g = j / 8). Their
+        // physical rows are loaded one stage ahead so that the loads' latency
+        // overlaps the wait for a free buffer.
+        int64_t ahead[4];
+        auto fetch = [&](int64_t first) {
+          const int n_f = (int)min((int64_t)R, seg_hi - first);
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const int r = 2 * (lane + 32 * (u >> 1)) + (u & 1);
+            ahead[u] = (r < R && r < n_f) ? __ldcg(rows + first + r) : -1;
+          }
+        };
+        fetch(seg_lo);
+        for (int64_t r0 = seg_lo; alive && r0 < seg_hi; r0 += R, ++t) {
+          const int st = t % kBulkStages;
+          if (!claim(st)) {
+            alive = false;
+            break;
+          }
+          char *kb = smem + st * sh.stage_bytes;
+          char *vb = kb + sh.plane_bytes;
+          int64_t now[4], src_off[4], blk[4], off[4];
+          bool ok[4];
+#pragma unroll
+          for (int u = 0; u < 4; ++u) now[u] = ahead[u];
+          if (r0 + R < seg_hi) fetch(r0 + R);
+          int nvalid = 0;
+          uint32_t bits[4] = {0u, 0u, 0u, 0u};
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            const int64_t row = now[u];
+            blk[u] = 0;
+            off[u] = 0;
+            if (row >= 0) {
+              if (p.page_shift >= 0) {
+                blk[u] = row >> p.page_shift;
+                off[u] = row & (p.page_size - 1);
+              } else {
+                blk[u] = row / p.page_size;
+                off[u] = row % p.page_size;
+              }
+            }
+            ok[u] = row >= 0 && blk[u] < p.pool_blocks;
+            if (row >= 0 && !ok[u]) flag(p.status, HS_DEV_ROW_OUT_OF_RANGE);
+            src_off[u] = (blk[u] * 2 * p.page_size + off[u]) * row_bytes;
+            nvalid += ok[u];
+            const int j = lane + 32 * (u >> 1);
+            const int sl = (j >> 3) * 16 + (j & 7) + (u & 1) * 8;
+#pragma unroll
+            for (int wi = 0; wi < 4; ++wi)
+              if (ok[u] && (sl >> 5) == wi) bits[wi] |= 1u << (sl & 31);
+          }
+          const int valid_total = warp_sum_int(nvalid);
+          if (lane == 0) mbar_add_tx(&full[st], (unsigned)(valid_total * 2 * row_bytes));
+          __syncwarp();
+#pragma unroll
+          for (int w = 0; w < 2; ++w) {
+            const int j = lane + 32 * w;
+            const int at = slot_offset(sh, (j >> 3) * 16 + (j & 7));  // its pair slot: + row_bytes
+            const int ua = 2 * w, ub = 2 * w + 1;
+            if (ok[ua] && ok[ub] && blk[ub] == blk[ua] && off[ub] == off[ua] + 1) {
+              // consecutive rows of one block: one copy of both K rows, one of both V rows
+              bulk_copy(kb + at, pool + src_off[ua], (unsigned)(2 * row_bytes), &full[st]);
+              bulk_copy(vb + at, pool + src_off[ua] + plane, (unsigned)(2 * row_bytes), &full[st]);
+            } else {
+              if (ok[ua]) {
+                bulk_copy(kb + at, pool + src_off[ua], (unsigned)row_bytes, &full[st]);
+                bulk_copy(vb + at, pool + src_off[ua] + plane, (unsigned)row_bytes, &full[st]);
+              }
+              if (ok[ub]) {
+                bulk_copy(kb + at + row_bytes, pool + src_off[ub], (unsigned)row_bytes,
+                          &full[st]);
+                bulk_copy(vb + at + row_bytes, pool + src_off[ub] + plane, (unsigned)row_bytes,
+                          &full[st]);
+              }
+            }
+          }
+          // slot masks; slots without data get a zeroed V row so that a zero
+          // weight cannot meet a NaN
+#pragma unroll
+          for (int wi = 0; wi < 4; ++wi) {
+            const uint32_t mask = __reduce_or_sync(kFullMask, bits[wi]);
+            if (lane == 0) info[st].ok[wi] = mask;
+            uint32_t bad = 32 * wi >= R ? 0u : ~mask;
+            if (32 * wi < R && 32 * wi + 32 > R) bad &= (1u << (R - 32 * wi)) - 1u;
+            while (bad) {
+              const int sl = 32 * wi + __ffs(bad) - 1;
+              bad &= bad - 1;
+              char *dst = vb + slot_offset(sh, sl);
+              for (int c = lane; c < sh.row_bytes / 16; c += 32)
+                *reinterpret_cast<uint4 *>(dst + c * 16) = make_uint4(0, 0, 0, 0);
+            }
+          }
+          if (valid_total < R) asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+          if (lane == 0) {
+            info[st].b = b;
+            info[st].slot = slot;
+            info[st].last = r0 + R >= seg_hi;
+          }
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&full[st]);
+        }
+      }
+      start += chunk_total;
+    }
+    // end record
+    if (alive) {
+      const int st = t % kBulkStages;
+      if (claim(st)) {
+        if (lane == 0) {
+          info[st].b = -1;
+          mbar_arrive(&full[st]);
+        }
+        ++t;
+      }
+    }
+    __syncwarp();
+    // no copy may still be landing when the CTA exits
+    if (lane == 0)
+      for (int u = max(0, t - kBulkStages); u < t; ++u)
+        mbar_wait(&full[u % kBulkStages], (u / kBulkStages) & 1, p.status);
+    return;
+  }
+
+  // ---------------- consumers ----------------
+  const int c = warp - 1;
+  const int kh = c % p.kv_heads, sub = c / p.kv_heads;
+  const int groups = p.q_heads / p.kv_heads;
+  const int h0 = kh * groups;
+  const int r0 = sub * 16;
+  const int gi = lane >> 3, rr = lane & 7;
+  constexpr float kLog2e = 1.4426950408889634f;
+  const float scale = p.scale * kLog2e;
+  uint32_t qb[8][2];
+  float m_ref[2], lsum[2], o[8][4];
+  auto reset = [&]() {
+    m_ref[0] = m_ref[1] = -INFINITY;
+    lsum[0] = lsum[1] = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+  };
+  reset();
+  // a barrier over the consumer warps whose wait is bounded (a warp that gave
+  // up on a stage cannot leave the others waiting for good)
+  unsigned xphase = 0;
+  auto consumers_sync = [&]() {
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&xbar);
+    mbar_wait(&xbar, xphase & 1, p.status);
+    ++xphase;
+  };
+  int cur_b = -1;
+  // slot of this lane's ldmatrix row: S^T reads slots r0 + rr (+8 for matrices
+  // 1, 3), O^T slots r0 + rr (+8 for matrices 2, 3)
+  const int k_row = slot_offset(sh, r0 + rr + (gi & 1) * 8);
+  const int v_row = slot_offset(sh, r0 + rr + (gi >> 1) * 8);
+  const int k_chunk = kh * 16 + (gi >> 1), v_chunk = kh * 16 + (gi & 1);
+  const int row_lo = r0 + (lane >> 2), row_hi = row_lo + 8;
+  for (int t = 0;; ++t) {
+    const int st = t % kBulkStages;
+    if (!mbar_wait(&full[st], (t / kBulkStages) & 1, p.status)) break;
+    const int b = info[st].b;
+    if (b < 0) break;
+    const int slot = info[st].slot;
+    const bool seg_end = info[st].last != 0;
+    const uint32_t okw_lo = info[st].ok[row_lo >> 5], okw_hi = info[st].ok[row_hi >> 5];
+    if (b != cur_b) {
+      cur_b = b;
+      const __nv_bfloat16 *qp =
+          static_cast<const __nv_bfloat16 *>(p.query) + (int64_t)b * p.query_batch_stride;
+      const int hq = lane >> 2;
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk) {
+        const int d = kk * 16 + (lane & 3) * 2;
+        const __nv_bfloat16 *qh = qp + (int64_t)(h0 + hq) * 128 + d;
+        qb[kk][0] = hq < groups ? *reinterpret_cast<const uint32_t *>(qh) : 0u;
+        qb[kk][1] = hq < groups ? *reinterpret_cast<const uint32_t *>(qh + 8) : 0u;
+      }
+    }
+    const char *kb = smem + st * sh.stage_bytes;
+    const char *vb = kb + sh.plane_bytes;
+    // ---- S^T = K Q^T (rows x heads) ----
+    float sa[4] = {0.f, 0.f, 0.f, 0.f}, sb[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int kk = 0; kk < 8; kk += 2) {
+      uint32_t a[4], a2[4];
+      ldmatrix_x4(smem_u32(kb + k_row + (k_chunk + 2 * kk) * 16), a[0], a[1], a[2], a[3]);
+      ldmatrix_x4(smem_u32(kb + k_row + (k_chunk + 2 * kk + 2) * 16), a2[0], a2[1], a2[2], a2[3]);
+      mma_bf16(sa, a, qb[kk][0], qb[kk][1]);
+      mma_bf16(sb, a2, qb[kk + 1][0], qb[kk + 1][1]);
+    }
+    const bool ok_lo = (okw_lo >> (row_lo & 31)) & 1u, ok_hi = (okw_hi >> (row_hi & 31)) & 1u;
+    float sv[4];
+    sv[0] = ok_lo ? (sa[0] + sb[0]) * scale : -INFINITY;  // slot lo, head 2*(lane%4)
+    sv[1] = ok_lo ? (sa[1] + sb[1]) * scale : -INFINITY;  // slot lo, head 2*(lane%4)+1
+    sv[2] = ok_hi ? (sa[2] + sb[2]) * scale : -INFINITY;  // slot hi
+    sv[3] = ok_hi ? (sa[3] + sb[3]) * scale : -INFINITY;
+    float mx0 = fmaxf(sv[0], sv[2]), mx1 = fmaxf(sv[1], sv[3]);
+#pragma unroll
+    for (int off = 4; off < 32; off <<= 1) {
+      mx0 = fmaxf(mx0, __shfl_xor_sync(kFullMask, mx0, off));
+      mx1 = fmaxf(mx1, __shfl_xor_sync(kFullMask, mx1, off));
+    }
+    const bool raise = mx0 > m_ref[0] + 8.f || mx1 > m_ref[1] + 8.f;
+    if (__any_sync(kFullMask, raise)) {
+      const float n0 = fmaxf(m_ref[0], mx0), n1 = fmaxf(m_ref[1], mx1);
+      const float a0 = m_ref[0] == -INFINITY ? 0.f : exp2f(m_ref[0] - n0);
+      const float a1 = m_ref[1] == -INFINITY ? 0.f : exp2f(m_ref[1] - n1);
+      lsum[0] *= a0;
+      lsum[1] *= a1;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        o[i][0] *= a0;
+        o[i][2] *= a0;
+        o[i][1] *= a1;
+        o[i][3] *= a1;
+      }
+      m_ref[0] = n0;
+      m_ref[1] = n1;
+    }
+    float pw[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float m = m_ref[e & 1];
+      pw[e] = (m == -INFINITY || sv[e] == -INFINITY) ? 0.f : exp2f(sv[e] - m);
+    }
+    lsum[0] += pw[0] + pw[2];
+    lsum[1] += pw[1] + pw[3];
+    const uint32_t bx = movmatrix_trans(pack_bf16(pw[0], pw[1]));  // P^T slots 0-7
+    const uint32_t by = movmatrix_trans(pack_bf16(pw[2], pw[3]));  // P^T slots 8-15
+    // ---- O^T += V^T P^T (head dim x heads) ----
+#pragma unroll
+    for (int mt = 0; mt < 8; ++mt) {
+      uint32_t a[4];
+      ldmatrix_x4_trans(smem_u32(vb + v_row + (v_chunk + 2 * mt) * 16), a[0], a[1], a[2], a[3]);
+      mma_bf16(o[mt], a, bx, by);
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[st]);
+    if (!seg_end) continue;
+    // ---- end of the segment: combine the warps of this KV head, write partials ----
+#pragma unroll
+    for (int e = 0; e < 2; ++e)
+#pragma unroll
+      for (int off = 4; off < 32; off <<= 1) lsum[e] += __shfl_xor_sync(kFullMask, lsum[e], off);
+    if (sh.subs > 1) {
+      float *xch = reinterpret_cast<float *>(smem + kBulkStages * sh.stage_bytes) +
+                   (kh * 32 + lane) * 36;
+      for (int round = 1; round < sh.subs; ++round) {
+        consumers_sync();
+        if (sub == round) {
+          xch[0] = m_ref[0];
+          xch[1] = m_ref[1];
+          xch[2] = lsum[0];
+          xch[3] = lsum[1];
+#pragma unroll
+          for (int i = 0; i < 8; ++i)
+#pragma unroll
+            for (int j = 0; j < 4; ++j) xch[4 + i * 4 + j] = o[i][j];
+        }
+        consumers_sync();
+        if (sub == 0) {
+          float f_me[2], f_it[2];
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const float mi = xch[e], mm = fmaxf(m_ref[e], mi);
+            f_me[e] = m_ref[e] == -INFINITY ? 0.f : exp2f(m_ref[e] - mm);
+            f_it[e] = mi == -INFINITY ? 0.f : exp2f(mi - mm);
+            lsum[e] = lsum[e] * f_me[e] + xch[2 + e] * f_it[e];
+            m_ref[e] = mm;
+          }
+#pragma unroll
+          for (int i = 0; i < 8; ++i)
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+              o[i][j] = o[i][j] * f_me[j & 1] + xch[4 + i * 4 + j] * f_it[j & 1];
+        }
+      }
+    }
+    if (sub == 0) {
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int hl = (lane & 3) * 2 + e;
+        if (hl >= groups) continue;
+        float *dst = partial_slot(p, b, h0 + hl, slot);
+        if ((lane >> 2) == 0) {
+          dst[128] = m_ref[e] * 0.6931471805599453f;  // log2 units -> natural log
+          dst[129] = lsum[e];
+        }
+#pragma unroll
+        for (int mt = 0; mt < 8; ++mt) {
+          dst[mt * 16 + (lane >> 2)] = o[mt][e];
+          dst[mt * 16 + (lane >> 2) + 8] = o[mt][2 + e];
+        }
+      }
+    }
+    reset();
+  }
+}
+
 // Merge: one 128-thread CTA per (request, query head). Thread t reads the
 // (max, sum) of partial t (phase 0's splits, then phase 1's; at most
 // 2 * kMaxSplits = 128 partials) and the block reduces the global max and the
@@ -512,7 +979,7 @@ __global__ void __launch_bounds__(kMergeThreads) attend_merge_kernel(AttendParam
   const int lane = t & 31, warp = t >> 5;
   const int D = p.head_dim, stride = D + 2;
   const bool even = (D & 1) == 0;
-  const int s0 = p.phase_splits[0], s1 = p.phases > 1 ? p.phase_splits[1] : 0;
+  const int s0 = p.phase_splits[b], s1 = p.phases > 1 ? p.phase_splits[p.batch + b] : 0;
   const int total = s0 + s1;
   p.phase = 0;
   const float *base0 = partial_slot(p, b, h, 0);
@@ -597,17 +1064,36 @@ __host__ inline int mma_splits(int batch, int64_t count, int stage_rows, int sms
   return (int)s;
 }
 
-// Upper bound of the splits either attention path uses (workspace sizing).
+// Partial slots per batch item the bulk path may use: an even spread of the
+// rows over the SMs gives an item at most ceil(sms / batch) + 1 of them.
+__host__ inline int bulk_slots(int batch, int sms) {
+  int64_t s = ceil_div((int64_t)sms, (int64_t)batch) + 2;
+  return (int)(s > kMaxSplits ? kMaxSplits : s);
+}
+
+// Upper bound of the partial slots any attention path uses (workspace sizing).
 __host__ inline int max_splits(int batch, int kv_heads, int64_t count, int sms) {
   const int a = attend_splits(batch, kv_heads, count, sms);
   const int m = mma_splits(batch, count, mma_shape(kv_heads).stage_rows, sms);
-  return a > m ? a : m;
+  const int k = bulk_slots(batch, sms);
+  return a > m ? (a > k ? a : k) : (m > k ? m : k);
 }
 
 template <typename TQ, typename TKV>
 int launch(AttendParams &p, cudaStream_t stream) {
   const int groups = p.q_heads / p.kv_heads;
   if constexpr (std::is_same<TQ, __nv_bfloat16>::value && std::is_same<TKV, __nv_bfloat16>::value) {
+    const bool kv_ok = p.kv_heads == 1 || p.kv_heads == 2 || p.kv_heads == 4 || p.kv_heads == 8;
+    if (p.head_dim == 128 && p.rows_head_stride == 0 && groups <= 8 && kv_ok &&
+        (reinterpret_cast<uintptr_t>(p.pool) & 15) == 0 &&
+        (reinterpret_cast<uintptr_t>(p.query) & 3) == 0 && (p.query_batch_stride & 1) == 0) {
+      const BulkShape sh = bulk_shape(p.kv_heads);
+      const int rc = reserve_smem((const void *)attend_bulk_kernel, sh.smem_bytes, "attend");
+      if (rc != HS_OK) return rc;
+      const int grid = sm_count() - p.spare_sms > 0 ? sm_count() - p.spare_sms : 1;
+      attend_bulk_kernel<<<grid, kBulkThreads, sh.smem_bytes, stream>>>(p);
+      return check_launch("attend_bulk_kernel");
+    }
     const int chunks16 = (groups + 15) / 16;
     if (p.head_dim == 128 && p.rows_head_stride == 0 && p.kv_heads * chunks16 <= kMmaWarps &&
         (reinterpret_cast<uintptr_t>(p.pool) & 15) == 0) {
@@ -656,7 +1142,7 @@ __global__ void __launch_bounds__(kNarrowThreads) attend_merge_narrow_kernel(Att
   const int h = blockIdx.x, b = blockIdx.y, t = threadIdx.x;
   const int lane = t & 31, warp = t >> 5;
   const int D = p.head_dim, stride = D + 2, d = blockIdx.z * 32 + lane;
-  const int s0 = p.phase_splits[0], s1 = p.phases > 1 ? p.phase_splits[1] : 0;
+  const int s0 = p.phase_splits[b], s1 = p.phases > 1 ? p.phase_splits[p.batch + b] : 0;
   const int total = s0 + s1;  // <= 2 * kMaxSplits
   p.phase = 0;
   const float *base0 = partial_slot(p, b, h, 0);
@@ -742,14 +1228,14 @@ template <typename TQ> int dispatch_kv(int kv_dtype, AttendParams &p, cudaStream
 namespace hs {
 namespace {
 
-// Workspace: partials of two phases, then the splits each phase used.
+// Workspace: partials of two phases, then the partials each phase left per batch item.
 struct AttendWorkspace {
   size_t partial_floats, bytes;
   int split_stride;
   AttendWorkspace(int batch, int q_heads, int kv_heads, int head_dim, int64_t count) {
     split_stride = max_splits(batch, kv_heads, count, sm_count());
     partial_floats = (size_t)2 * batch * q_heads * split_stride * (head_dim + 2);
-    bytes = partial_floats * sizeof(float) + 2 * sizeof(int);
+    bytes = partial_floats * sizeof(float) + (size_t)2 * batch * sizeof(int);
   }
 };
 
@@ -870,6 +1356,7 @@ extern "C" int hs_attend_rows_phase(int batch, const void *query, int64_t query_
                    workspace, workspace_bytes, device_status);
   if (rc != HS_OK) return rc;
   p.phase = phase;
+  p.spare_sms = kPhaseSpareSms;
   p.valid_counts = valid_counts;
   p.counts_stride = counts_stride;
   p.counts_first = counts_first;

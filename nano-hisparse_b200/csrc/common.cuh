@@ -193,4 +193,65 @@ struct Lengths {
   }
 };
 
+// ---- mbarriers and 1-D bulk copies (the TMA engine's untiled form) ----------------
+// Every wait is bounded: kWaitLimit tries, each of which may suspend the warp for
+// up to ~1 ms until the phase completes (about 4 s in all), after which the
+// caller sets HS_DEV_WAIT_TIMEOUT and winds down. No copy here uses cluster
+// multicast.
+constexpr long long kWaitLimit = 4000;
+
+__device__ __forceinline__ uint32_t smem_addr(const void *p) {
+  return (uint32_t)__cvta_generic_to_shared(p);
+}
+__device__ __forceinline__ void mbar_init(uint64_t *bar, unsigned count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(smem_addr(bar)), "r"(count));
+}
+// Arrive (one of the phase's expected arrivals) and add `bytes` to the
+// transaction count that the phase's bulk copies will complete.
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, unsigned bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(smem_addr(bar)),
+               "r"(bytes)
+               : "memory");
+}
+// Add `bytes` to the phase's transaction count without arriving.
+__device__ __forceinline__ void mbar_add_tx(uint64_t *bar, unsigned bytes) {
+  asm volatile("mbarrier.expect_tx.relaxed.cta.shared::cta.b64 [%0], %1;\n" ::"r"(smem_addr(bar)),
+               "r"(bytes)
+               : "memory");
+}
+// Plain arrive (release: the caller's earlier shared-memory writes are visible
+// to the threads that wait for the phase).
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(smem_addr(bar)) : "memory");
+}
+// try_wait with a suspend-time hint: the warp sleeps until the phase
+// completes (or about 1 ms passes) instead of spinning through instructions.
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, unsigned parity) {
+  unsigned done;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n"
+      " selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(done)
+      : "r"(smem_addr(bar)), "r"(parity), "r"(1000000u)
+      : "memory");
+  return done != 0;
+}
+// Global -> this CTA's shared memory, completing `bytes` on `bar`. Both
+// addresses 16-byte aligned, bytes a multiple of 16.
+__device__ __forceinline__ void bulk_copy(void *dst, const void *src, unsigned bytes,
+                                          uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n"
+      ::"r"(smem_addr(dst)), "l"(src), "r"(bytes), "r"(smem_addr(bar))
+      : "memory");
+}
+// Waits for `parity` of `bar`; false (and a device flag) when the bounded
+// wait runs out.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, unsigned parity, int32_t *status) {
+  for (long long i = 0; i < kWaitLimit; ++i)
+    if (mbar_try_wait(bar, parity)) return true;
+  flag(status, HS_DEV_WAIT_TIMEOUT);
+  return false;
+}
+
 }  // namespace hs

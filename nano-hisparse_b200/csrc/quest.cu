@@ -492,47 +492,6 @@ constexpr int kTmaThreads = 512;
 constexpr int kTmaWarps = kTmaThreads / 32;
 constexpr int kTmaStagePages = 16;
 constexpr int kTmaStages = 3;
-constexpr long long kWaitLimit = 4000;  // bounded mbarrier waits (each suspends up to ~1 ms)
-
-__device__ __forceinline__ uint32_t smem_addr(const void *p) {
-  return (uint32_t)__cvta_generic_to_shared(p);
-}
-__device__ __forceinline__ void mbar_init(uint64_t *bar, unsigned count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(smem_addr(bar)), "r"(count));
-}
-__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, unsigned bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(smem_addr(bar)),
-               "r"(bytes)
-               : "memory");
-}
-// try_wait with a suspend-time hint: the warp sleeps until the phase
-// completes (or about 1 ms passes) instead of spinning through instructions.
-__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, unsigned parity) {
-  unsigned done;
-  asm volatile(
-      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n"
-      " selp.u32 %0, 1, 0, p;\n}\n"
-      : "=r"(done)
-      : "r"(smem_addr(bar)), "r"(parity), "r"(1000000u)
-      : "memory");
-  return done != 0;
-}
-__device__ __forceinline__ void bulk_copy(void *dst, const void *src, unsigned bytes,
-                                          uint64_t *bar) {
-  asm volatile(
-      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n"
-      ::"r"(smem_addr(dst)), "l"(src), "r"(bytes), "r"(smem_addr(bar))
-      : "memory");
-}
-// Waits for `parity` of `bar`; false (and a device flag) when the bounded
-// wait runs out.
-__device__ __forceinline__ bool mbar_wait(uint64_t *bar, unsigned parity, int32_t *status) {
-  for (long long i = 0; i < kWaitLimit; ++i)
-    if (mbar_try_wait(bar, parity)) return true;
-  flag(status, HS_DEV_WAIT_TIMEOUT);
-  return false;
-}
-
 template <typename TQ, typename TKV, int C>
 __global__ void __launch_bounds__(kTmaThreads, 1) quest_tma_kernel(QuestParams<TQ, TKV> p) {
   extern __shared__ __align__(128) char smem[];

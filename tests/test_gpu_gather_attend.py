@@ -152,3 +152,79 @@ def test_attention_all_rows_invalid_gives_zeros():
     out = attend_rows(torch.randn(2, 8, device=DEV), pool, torch.full((4,), -1, device=DEV),
                       _config(pool))
     assert out.abs().sum().item() == 0
+
+
+def _phase_attention(q, pool, counts, phases):
+    """hs_attend_rows_phase over the leading valid rows of each phase's rows
+    ([B, K]) selected by a (first, n) component range of `counts` ([B, 3]),
+    then hs_attend_merge."""
+    lib = _lib.load()
+    b, hq, d = q.shape
+    _, _, p, hkv, _ = pool.shape
+    k = phases[0][0].shape[1]
+    out = torch.empty_like(q)
+    nbytes = lib.hs_attend_workspace_bytes(b, hq, hkv, d, k)
+    ws = torch.empty(nbytes, dtype=torch.uint8, device=DEV)
+    status, stream = _lib.status_word(DEV).data_ptr(), torch.cuda.current_stream().cuda_stream
+    code = _lib.dtype_code(q.dtype)
+    for phase, (r, first, n) in enumerate(phases):
+        _lib.check(lib.hs_attend_rows_phase(
+            b, q.data_ptr(), hq * d, code, pool.data_ptr(), pool.shape[0], code, r.data_ptr(),
+            k, k, counts.data_ptr(), 3, first, n, phase, hq, hkv, d, p, ws.data_ptr(), nbytes,
+            status, stream))
+    _lib.check(lib.hs_attend_merge(b, len(phases), out.data_ptr(), hq * d, code, hq, hkv, d, k,
+                                   ws.data_ptr(), nbytes, status, stream))
+    return out
+
+
+@pytest.mark.parametrize("hq,hkv,b,k", [
+    (32, 8, 8, 2048),    # configuration 2 shape, 8 requests of a micro-batch
+    (28, 4, 1, 8192),    # configuration 5 on one GPU
+    (14, 2, 1, 8192),    # configuration 5, heads split over 2 ranks
+    (7, 1, 1, 8192),     # configuration 5, heads split over 4 ranks
+    (32, 8, 64, 512),    # a wide batch
+    (8, 8, 5, 300),      # one query head per KV head
+    (16, 2, 3, 1000),    # eight query heads per KV head
+])
+def test_attention_two_phase_uneven_requests(hq, hkv, b, k):
+    """The two-phase attention (ready rows, then gathered rows, then the merge)
+    over requests with uneven, empty and full valid counts, rows both in whole
+    pages (consecutive pool rows) and scattered: every request's output equals
+    the oracle's attention over its valid rows of both phases."""
+    gen = torch.Generator().manual_seed(hq * 100 + b)
+    d, p = 128, 16
+    blocks = 4 * k // p + 8
+    pool = torch.randn(blocks, 2, p, hkv, d, generator=gen).to(torch.bfloat16)
+    q = torch.randn(b, hq, d, generator=gen).to(torch.bfloat16)
+
+    def rows_like_a_selection():
+        # whole pages (runs of consecutive rows) for the first half, single rows after
+        pages = torch.randperm(blocks, generator=gen)[:k // (2 * p) + 1]
+        runs = (pages[:, None] * p + torch.arange(p)).reshape(-1)[:k // 2]
+        single = torch.randperm(blocks * p, generator=gen)[:k - runs.numel()]
+        return torch.cat([runs, single])
+
+    ready = torch.stack([rows_like_a_selection() for _ in range(b)])
+    missed = torch.stack([torch.randperm(blocks * p, generator=gen)[:k] for _ in range(b)])
+    counts = torch.zeros(b, 3, dtype=torch.int64)
+    for i in range(b):
+        kind = i % 4
+        r_hits = [k, 0, k // 3, 1][kind] if b > 1 else k * 3 // 4
+        misses = [0, k, k // 5, k - 1][kind] if b > 1 else k // 4
+        counts[i] = torch.tensor([r_hits // 2, r_hits - r_hits // 2, misses])
+    if b > 2:
+        counts[2] = 0                      # an empty request
+    ready[0, 3] = -1                        # a skipped row inside the valid range
+    dq, dpool = q.to(DEV), pool.to(DEV)
+    dready, dmissed, dcounts = ready.to(DEV), missed.to(DEV), counts.to(DEV)
+    out = _phase_attention(dq, dpool, dcounts, [(dready, 0, 2), (dmissed, 2, 1)])
+    for i in range(b):
+        nr, nm = int(counts[i, :2].sum()), int(counts[i, 2])
+        rows = torch.cat([ready[i, :nr], missed[i, :nm]])
+        if rows.numel() == 0 or (rows < 0).all():
+            assert out[i].abs().sum().item() == 0, i
+            continue
+        ref = oracle.attend_rows(q[i], pool, rows.numpy(), p)
+        torch.testing.assert_close(out[i].cpu().double(), torch.from_numpy(ref),
+                                   **TOL[torch.bfloat16], msg=f"request {i}")
+    assert not _lib.device_flags(DEV)
