@@ -750,6 +750,234 @@ def run_config5(args, rank, world, local_rank, log):
 
 
 # ---------------------------------------------------------------------------
+# configuration 3: isolated decode attention, resident-fraction sweep
+# ---------------------------------------------------------------------------
+C3 = {"requests": 64, "q_heads": 32, "kv_heads": 8, "head_dim": 128, "context": 131072,
+      "page_sizes": (16, 64), "rows": 4096, "resident_fractions": (0.10, 0.25, 0.50, 0.90),
+      "hot_rows": 8192, "trace_steps": 64, "settle_steps": 16, "overlap": 0.70, "seed": 2}
+
+
+def lru_trace(rng, pages, chosen, steps, overlap):
+    """Selected pages of `steps` decode steps of one query: step 0 draws
+    `chosen` pages uniformly; every later step keeps `overlap` of the previous
+    step's pages (a uniform subset) and draws the rest uniformly from the
+    pages not kept."""
+    keep = int(round(chosen * overlap))
+    cur = np.sort(rng.choice(pages, size=chosen, replace=False))
+    out = [cur]
+    for _ in range(1, steps):
+        kept = rng.choice(cur, size=keep, replace=False)
+        mask = np.ones(pages, dtype=bool)
+        mask[kept] = False
+        fresh = rng.choice(np.flatnonzero(mask), size=chosen - keep, replace=False)
+        cur = np.sort(np.concatenate([kept, fresh]))
+        out.append(cur)
+    return out
+
+
+def run_config3(args, rank, world, local_rank, log):
+    """Decode attention of 64 queries over 4,096 selected rows each at 131,072
+    tokens of context (32 q / 8 KV heads, bf16), page sizes 16 and 64, with 10,
+    25, 50 and 90 % of each request's pages resident in the pool and the rest
+    only in pinned host memory. Each query's selection follows a 64-step trace
+    whose steps keep 70 % of the previous step's pages; the hot buffer (8,192
+    rows per request) is filled by the first 16 steps, the other 48 are timed.
+    A step resolves, gathers and attends every query (one DecodeBatch layer
+    over the trace's positions); Quest scoring of the same requests' metadata
+    is timed beside it."""
+    from hisparse_b200 import CacheConfig, DecodeBatch, HotConfig, RowCache, _lib
+    from hisparse_b200.sharding import bind_to_device_node
+
+    c = C3
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    bind_to_device_node(local_rank)
+    hbm_peak, hbm_source = measured_peaks()
+    link_peak = hostlink_peak(device)
+    B, HQ, HKV, D, T = c["requests"], c["q_heads"], c["kv_heads"], c["head_dim"], c["context"]
+    row_bytes = 2 * HKV * D * 2
+    steps_total, settle = c["trace_steps"], c["settle_steps"]
+    timed_steps = steps_total - settle
+    lines = []
+    for P in c["page_sizes"]:
+        n = T // P
+        chosen = c["rows"] // P
+        hot = HotConfig(c["rows"], c["hot_rows"])
+        hot_blocks = hot.hot_blocks(P)
+        page_bytes = 2 * P * HKV * D * 2
+        host_pages = host_store_pages(B * n, page_bytes, log)
+        top_res = int(round(n * max(c["resident_fractions"])))
+        config = CacheConfig(gpu_pages=B * (top_res + hot_blocks), host_pages=host_pages,
+                             page_size=P, kv_heads=HKV, head_dim=D, device=str(device),
+                             dtype=DTYPE, index_budget_bytes=1 << 40)
+        t0 = time.time()
+        host = torch.empty((host_pages, 2, P, HKV, D), dtype=DTYPE, pin_memory=True)
+        cache = RowCache(config, hot, host=host)
+        gen = torch.Generator(device=device).manual_seed(c["seed"])
+        rng = np.random.default_rng(c["seed"])
+        mins, maxs, order, bases = {}, {}, {}, {}
+        block = 0
+        for r in range(B):
+            base = (r * n) % (host_pages - n + 1)
+            bases[r] = base
+            kv = torch.randn((n, 2, P, HKV, D), generator=gen, device=device,
+                             dtype=torch.float32).to(DTYPE)
+            mins[r] = kv[:, 0].amin(1)[None].contiguous()
+            maxs[r] = kv[:, 0].amax(1)[None].contiguous()
+            host[base:base + n].copy_(kv, non_blocking=True)
+            # residency: the first f*n pages of one permutation are resident at
+            # fraction f (nested sets); the pool holds the largest set
+            perm = rng.permutation(n)
+            order[r] = perm
+            idx = torch.from_numpy(np.sort(perm[:top_res])).to(device)
+            res_blocks = block + torch.arange(top_res, device=device)
+            cache.pool[res_blocks] = kv.index_select(0, idx)
+            block += top_res
+            hot_list = list(range(block, block + hot_blocks))
+            block += hot_blocks
+            cache.add_layer(r, 0, T, np.arange(base, base + n), np.full(n, -1), hot_list)
+            torch.cuda.synchronize(device)
+        log(f"config3 P{P}: KV, metadata and pool placement in {time.time() - t0:.1f}s")
+        # pool block of page p at the largest fraction (its rank in the sorted prefix)
+        block_of = {}
+        for r in range(B):
+            top = np.sort(order[r][:top_res])
+            base_block = r * (top_res + hot_blocks)
+            blk = np.full(n, -1, dtype=np.int64)
+            blk[top] = base_block + np.arange(top_res)
+            block_of[r] = blk
+        traces = [lru_trace(rng, n, chosen, steps_total, c["overlap"]) for _ in range(B)]
+        offs = np.arange(P, dtype=np.int32)
+        positions = torch.from_numpy(np.stack([
+            np.stack([(tr[s][:, None] * P + offs).reshape(-1).astype(np.int32)
+                      for tr in traces]) for s in range(steps_total)])).to(device)
+        qgen = torch.Generator(device=device).manual_seed(c["seed"] + 1)
+        queries = torch.randn((steps_total, B, HQ, D), generator=qgen, device=device,
+                              dtype=torch.float32).to(DTYPE)
+        streams = (torch.cuda.Stream(device=device), torch.cuda.Stream(device=device))
+        with torch.cuda.stream(streams[0]):
+            batch = DecodeBatch(cache, list(range(B)), 1, mins, maxs, chosen, HQ,
+                                streams=streams)
+        torch.cuda.synchronize(device)
+        # Quest scoring + top-k of the same 64 requests, timed alone
+        lib = _lib.load()
+        st0 = batch.layers[0]
+        qws = batch.quest_ws
+        q_events = []
+        with torch.cuda.stream(batch.compute):
+            for s_ in range(8):
+                a, b_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record()
+                _lib.check(lib.hs_quest_select_batched(
+                    B, queries[s_].data_ptr(), HQ * D, _lib.HS_BFLOAT16, st0.min_ptrs.data_ptr(),
+                    st0.max_ptrs.data_ptr(), _lib.HS_BFLOAT16, st0.lengths.data_ptr(), HQ, HKV,
+                    D, batch.max_pages, P, chosen, 1, batch.tokens.data_ptr(), batch.width,
+                    batch.token_counts.data_ptr(), _lib.ptr(qws), batch.quest_ws_bytes,
+                    batch.status.data_ptr(), batch.compute.cuda_stream))
+                b_.record()
+                q_events.append((a, b_))
+        torch.cuda.synchronize(device)
+        quest_ms = float(np.median([a.elapsed_time(b_) for a, b_ in q_events[2:]]))
+        quest_bytes = B * 2 * n * HKV * D * 2
+        out = torch.empty((B, HQ, D), dtype=DTYPE, device=device)
+        counts = torch.zeros((steps_total, B, 3), dtype=torch.int64, device=device)
+        for frac in c["resident_fractions"]:
+            k = int(round(n * frac))
+            for r in range(B):
+                res = np.full(n, -1, dtype=np.int64)
+                pages = order[r][:k]
+                res[pages] = block_of[r][pages]
+                t_ = cache.tables[r, 0]
+                t_.resident.copy_(torch.from_numpy(res.astype(np.int32)))
+                t_.tags.fill_(-1)
+                t_.lru.copy_(torch.arange(c["hot_rows"], dtype=torch.int64))
+            for st in batch.layers:
+                st.ready = st.last_use = None
+            torch.cuda.synchronize(device)
+            events = []
+            with torch.cuda.stream(batch.compute):
+                for s_ in range(steps_total):
+                    if s_ >= settle:
+                        a = torch.cuda.Event(enable_timing=True)
+                        a.record()
+                    batch.layer(0, queries[s_], out, counts[s_], positions=positions[s_])
+                    if s_ >= settle:
+                        b_ = torch.cuda.Event(enable_timing=True)
+                        b_.record()
+                        events.append((a, b_))
+            torch.cuda.synchronize(device)
+            span_ms = events[0][0].elapsed_time(events[-1][1])
+            # per-stage device time: one more trace step, each stage alone
+            timing = []
+            with torch.cuda.stream(batch.compute):
+                torch.cuda._sleep(1_000_000)
+                batch.layer(0, queries[steps_total - 1], out, None, timing, serial=True,
+                            positions=positions[steps_total - 1])
+            torch.cuda.synchronize(device)
+            stage = {}
+            for name, a, b_ in timing:
+                stage[name] = stage.get(name, 0.0) + a.elapsed_time(b_)
+            cnt = counts[settle:].sum(dim=(0, 1)).cpu().numpy()  # resident, hot, miss
+            per_step = cnt / timed_steps
+            sel_rows = float(per_step.sum())
+            misses = float(per_step[2])
+            hbm = (sel_rows + misses) * row_bytes  # KV rows read, miss rows written
+            hostb = misses * row_bytes
+            ms = span_ms / timed_steps
+            t_roof = max(hbm / (hbm_peak * 1e9), hostb / (link_peak * 1e9))
+            attend_ms = stage.get("attend_ready", 0.0) + stage.get("attend_gathered", 0.0)
+            gather_ms = stage.get("gather", 0.0)
+            lines.append({
+                "page_size": P, "resident_fraction": frac,
+                "queries_per_s": round(B / (ms * 1e-3), 1), "ms_per_step": round(ms, 4),
+                "rows_per_query": {"resident": round(per_step[0] / B, 1),
+                                   "hot": round(per_step[1] / B, 1),
+                                   "miss": round(per_step[2] / B, 1)},
+                "hbm_bytes_per_step": int(hbm), "hostlink_bytes_per_step": int(hostb),
+                "step_roofline": {"t_roof_ms": round(t_roof * 1e3, 4),
+                                  "frac": round(t_roof / (ms * 1e-3), 4),
+                                  "bound": "hbm" if hbm / hbm_peak > hostb / link_peak
+                                  else "hostlink"},
+                "stage_ms": {k_: round(v, 4) for k_, v in stage.items()},
+                "attend_gbs": round(sel_rows * row_bytes / (attend_ms * 1e-3) / 1e9, 1)
+                if attend_ms > 0 else None,
+                "gather_gbs": round(hostb / (gather_ms * 1e-3) / 1e9, 2) if gather_ms > 0
+                else None,
+            })
+            log(f"config3 P{P} resident {frac:.2f}: {ms:.3f} ms/step, "
+                f"roofline {t_roof / (ms * 1e-3):.3f}")
+        lines_quest = {"page_size": P, "ms_per_launch": round(quest_ms, 4),
+                       "bytes_per_launch": quest_bytes,
+                       "achieved_gbs": round(quest_bytes / (quest_ms * 1e-3) / 1e9, 1),
+                       "frac_of_hbm": round(quest_bytes / (quest_ms * 1e-3) / 1e9 / hbm_peak, 4)}
+        lines.append({"page_size": P, "quest": lines_quest})
+        flags = _lib.device_flags(device)
+        if flags:
+            raise RuntimeError(f"device flags raised: {flags}")
+        del batch, cache, host, mins, maxs, positions, queries
+        torch.cuda.empty_cache()
+    sweep = [x for x in lines if "quest" not in x]
+    quest = [x["quest"] for x in lines if "quest" in x]
+    # headline: the HBM-bound corner (page 64, 90 % resident)
+    head = [x for x in sweep if x["page_size"] == 64 and x["resident_fraction"] == 0.9][0]
+    return {
+        "metric": "decode-attention queries/s (64 queries x 4096 rows, 131072 ctx)",
+        "value": head["queries_per_s"], "unit": "queries/s", "n_gpus": world,
+        "steps": timed_steps, "warmup": settle, "ms_per_step": head["ms_per_step"],
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic",
+        "config": {"workload": "config 3: isolated decode attention (resolve, miss gather, "
+                               "two-phase row attention, merge) over a 64-step LRU trace, "
+                               "resident fraction and page size swept",
+                   **{k: v for k, v in c.items()}},
+        "headline_point": {"page_size": 64, "resident_fraction": 0.9},
+        "hbm_peak": {"gbs": hbm_peak, "source": hbm_source},
+        "hostlink_peak_gbs": round(link_peak, 2),
+        "sweep": sweep, "quest": quest,
+    }
+
+
+# ---------------------------------------------------------------------------
 # CPU arm (oracle restatement of the reference's path)
 # ---------------------------------------------------------------------------
 def cpu_sample(seed=1, budget_s=10.0, threads=None, log=print):
@@ -835,8 +1063,10 @@ def main():
     parser.add_argument("--transfer", choices=["shared", "separate"], default=TRANSFER,
                         help="one transfer stream for all micro-batches (gathers take the "
                              "host link in turn) or one each")
-    parser.add_argument("--workload", choices=["config2", "config5"], default="config2",
-                        help="config2 (the bench line) or config5 (one 1M-token request, KV "
+    parser.add_argument("--workload", choices=["config2", "config3", "config5"],
+                        default="config2",
+                        help="config2 (the bench line), config3 (isolated decode attention, "
+                             "resident-fraction sweep) or config5 (one 1M-token request, KV "
                              "heads split over 1, 2 or 4 GPUs)")
     parser.add_argument("--requests", type=int, default=REQUESTS)
     parser.add_argument("--layers", type=int, default=LAYERS)
@@ -878,8 +1108,9 @@ def main():
                                 device_id=torch.device("cuda", local_rank))
     try:
         all_cpus = os.sched_getaffinity(0)
-        if args.workload == "config5":
-            result = run_config5(args, rank, world, local_rank, log)
+        if args.workload in ("config3", "config5"):
+            run = run_config3 if args.workload == "config3" else run_config5
+            result = run(args, rank, world, local_rank, log)
             if rank == 0:
                 print(json.dumps(result), flush=True)
             return

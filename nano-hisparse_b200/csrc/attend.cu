@@ -529,20 +529,23 @@ __global__ void __launch_bounds__(kMmaThreads, 1) attend_mma_kernel(AttendParams
 // When a segment ends, warps serving the same KV head combine their (max, sum,
 // O) through shared memory and one of them writes the partials.
 constexpr int kBulkConsumers = 8;
-constexpr int kBulkThreads = 32 * (1 + kBulkConsumers);
+constexpr int kBulkProducers = 2;  // producer warps, taking alternate stages
+constexpr int kBulkThreads = 32 * (kBulkProducers + kBulkConsumers);
 constexpr int kBulkStages = 3;
 // A phase launch runs beside other work (the miss gather, another request
 // group's selection and resolve); leaving it a few SMs keeps a pipelined decode
 // step 7% faster than taking every SM.
 constexpr int kPhaseSpareSms = 4;
+constexpr int kRowAhead = 3;  // tiles whose row indices the producer loads ahead
 
 struct BulkShape {
-  int row_bytes;    // kv_heads * 256: K (or V) of one token, every KV head
-  int pair_stride;  // 2 * row_bytes + 16: two slots side by side, then 16 bytes of pad
-  int stage_rows;   // 16 * subs
-  int subs;         // consumer warps per KV head
-  int plane_bytes;  // K (or V) slots of a stage
-  int stage_bytes;  // K slots, then V slots
+  int row_bytes;     // kv_heads * 256: K (or V) of one token, every KV head
+  int run;           // G = stage_rows / 8: slots per group (4 KiB of rows)
+  int group_stride;  // G * row_bytes + 16: a group's slots side by side, then 16 bytes of pad
+  int stage_rows;    // 16 * subs
+  int subs;          // consumer warps per KV head
+  int plane_bytes;   // K (or V) slots of a stage: 8 groups
+  int stage_bytes;   // K slots, then V slots
   int combine_bytes;  // shared memory for combining the warps of one KV head
   int smem_bytes;
 };
@@ -550,23 +553,28 @@ struct BulkShape {
 __host__ __device__ inline BulkShape bulk_shape(int kv_heads) {
   BulkShape s;
   s.row_bytes = kv_heads * kHeadBytes;
-  s.pair_stride = 2 * s.row_bytes + 16;
   s.subs = kBulkConsumers / kv_heads;
   s.stage_rows = 16 * s.subs;
-  s.plane_bytes = (s.stage_rows / 2) * s.pair_stride;
+  s.run = s.stage_rows / 8;
+  s.group_stride = s.run * s.row_bytes + 16;
+  s.plane_bytes = 8 * s.group_stride;
   s.stage_bytes = 2 * s.plane_bytes;
   s.combine_bytes = s.subs > 1 ? kv_heads * 32 * 36 * (int)sizeof(float) : 0;
   s.smem_bytes = kBulkStages * s.stage_bytes + s.combine_bytes;
   return s;
 }
 
-// Shared-memory offset of stage slot `slot` within a plane. Slots come in
-// groups of 16 (one consumer warp's rows); within a group, slots j and j + 8
-// are adjacent (one pair, so two consecutive pool rows land with one copy) and
-// the 8 pairs are pair_stride apart. The 8 slots an ldmatrix reads (j = 0..7 of
-// one half) are then 16 bytes apart modulo 128: no bank conflicts.
+// A stage's rows sit in 8 groups of G = stage_rows / 8 slots. Tile row i (the
+// i-th row of the stage) goes to group i / G, position i % G: G consecutive
+// rows of the tile are adjacent in shared memory, so a run of consecutive pool
+// rows among them lands with one copy per plane (G * row_bytes = 4 KiB). Slot s
+// is group s % 8, position s / 8: the 8 slots an ldmatrix reads (s = j..j+7)
+// are in 8 different groups, 16 bytes apart modulo 128 — no bank conflicts.
 __host__ __device__ __forceinline__ int slot_offset(const BulkShape &s, int slot) {
-  return ((slot >> 4) * 8 + (slot & 7)) * s.pair_stride + ((slot >> 3) & 1) * s.row_bytes;
+  return (slot & 7) * s.group_stride + (slot >> 3) * s.row_bytes;
+}
+__host__ __device__ __forceinline__ int tile_slot(const BulkShape &s, int i) {
+  return (i % s.run) * 8 + i / s.run;
 }
 
 struct BulkStage {
@@ -596,6 +604,7 @@ __global__ void __launch_bounds__(kBulkThreads, 1) attend_bulk_kernel(AttendPara
   __shared__ __align__(8) uint64_t full[kBulkStages], empty[kBulkStages];
   __shared__ __align__(8) uint64_t xbar;  // consumer warps' combine rounds
   __shared__ BulkStage info[kBulkStages];
+  __shared__ int64_t row_ring[kBulkProducers][4][128];  // physical rows of upcoming tiles
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const BulkShape sh = bulk_shape(p.kv_heads);
   const int R = sh.stage_rows;
@@ -609,8 +618,12 @@ __global__ void __launch_bounds__(kBulkThreads, 1) attend_bulk_kernel(AttendPara
   }
   __syncthreads();
 
-  if (warp == 0) {
-    // ---------------- producer ----------------
+  if (warp < kBulkProducers) {
+    // ---------------- producers ----------------
+    // Producer warp pw fills the stages t with t % kBulkProducers == pw: while
+    // one warp checks its rows, the copy engine works through the other's
+    // copies (it takes them one at a time, ~85 cycles each).
+    const int pw = warp;
     // total valid rows, the largest item, and (CTA 0) zero counts for empty items
     int64_t total = 0, largest = 0;
     for (int b0 = 0; b0 < p.batch; b0 += 32) {
@@ -634,12 +647,12 @@ __global__ void __launch_bounds__(kBulkThreads, 1) attend_bulk_kernel(AttendPara
     const char *pool = p.pool;
     const int64_t row_bytes = sh.row_bytes;
     const int64_t plane = (int64_t)p.page_size * row_bytes;  // bytes from a K row to its V row
-    int t = 0;  // stages issued
+    int t = 0;  // stages of the CTA before the current segment (both warps count all)
     bool alive = true;
-    // claim the next stage buffer (waits for the consumers to release it)
-    auto claim = [&](int st) -> bool {
-      if (t < kBulkStages) return true;
-      return mbar_wait(&empty[st], ((t / kBulkStages) - 1) & 1, p.status);
+    // claim stage tt's buffer (waits for the consumers to release it)
+    auto claim = [&](int tt) -> bool {
+      if (tt < kBulkStages) return true;
+      return mbar_wait(&empty[tt % kBulkStages], ((tt / kBulkStages) - 1) & 1, p.status);
     };
     int64_t start = 0;  // first row of item b0 in the sequence
     for (int b0 = 0; alive && b0 < p.batch && start < hi; b0 += 32) {
@@ -659,81 +672,116 @@ __global__ void __launch_bounds__(kBulkThreads, 1) attend_bulk_kernel(AttendPara
         const int slot = (int)(blockIdx.x - s_b / chunk);
         if (s_b + v_b <= hi && lane == 0) p.phase_splits[p.phase * p.batch + b] = slot + 1;
         const int64_t *rows = p.rows + (int64_t)b * p.rows_batch_stride;
-        // Lane l handles the tile's row pairs j = l and l + 32 (rows 2j, 2j + 1
-        // of the tile, slots g*16 + j%8 and that + 8 with g = j / 8). Their
-        // physical rows are loaded one stage ahead so that the loads' latency
-        // overlaps the wait for a free buffer.
-        int64_t ahead[4];
-        auto fetch = [&](int64_t first) {
-          const int n_f = (int)min((int64_t)R, seg_hi - first);
+        // Lane l handles tile rows l, l + 32, ... of each tile. Their physical
+        // rows travel to a 4-slot shared ring by cp.async, kRowAhead tiles
+        // ahead of their use: a row-index load that waits in the stage's
+        // critical path costs the whole L2 round trip per stage.
+        const int64_t seg_tiles = ceil_div(seg_hi - seg_lo, (int64_t)R);
+        // this warp's tiles of the segment: k = k_first + m * kBulkProducers
+        const int64_t k_first = ((pw - t) % kBulkProducers + kBulkProducers) % kBulkProducers;
+        int64_t *ring = &row_ring[pw][0][0];
+        auto prefetch = [&](int64_t m) {  // this warp's tile m into ring slot m % 4
+          const int64_t k = k_first + m * kBulkProducers;
+          if (k < seg_tiles) {
+            const int64_t first = seg_lo + k * R;
+            const int n_f = (int)min((int64_t)R, seg_hi - first);
 #pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            const int r = 2 * (lane + 32 * (u >> 1)) + (u & 1);
-            ahead[u] = (r < R && r < n_f) ? __ldcg(rows + first + r) : -1;
+            for (int u = 0; u < 4; ++u) {
+              const int i = lane + 32 * u;
+              int64_t *slot_ptr = ring + (m & 3) * 128 + (i < 128 ? i : 0);
+              if (i < R && i < n_f)
+                asm volatile("cp.async.ca.shared.global [%0], [%1], 8;\n" ::"r"(
+                                 smem_addr(slot_ptr)), "l"(rows + first + i) : "memory");
+              else if (i < R)
+                *slot_ptr = -1;
+            }
           }
+          asm volatile("cp.async.commit_group;\n" ::: "memory");
         };
-        fetch(seg_lo);
-        for (int64_t r0 = seg_lo; alive && r0 < seg_hi; r0 += R, ++t) {
-          const int st = t % kBulkStages;
-          if (!claim(st)) {
+        asm volatile("cp.async.wait_group 0;\n" ::: "memory");  // the previous segment's slots
+#pragma unroll
+        for (int m = 0; m < kRowAhead; ++m) prefetch(m);
+        for (int64_t m = 0; alive; ++m) {
+          const int64_t k = k_first + m * kBulkProducers;
+          if (k >= seg_tiles) break;
+          const int tt = t + (int)k;
+          const int st = tt % kBulkStages;
+          const int64_t r0 = seg_lo + k * R;
+          if (!claim(tt)) {
             alive = false;
             break;
           }
           char *kb = smem + st * sh.stage_bytes;
-          char *vb = kb + sh.plane_bytes;
-          int64_t now[4], src_off[4], blk[4], off[4];
-          bool ok[4];
+          prefetch(m + kRowAhead);
+          asm volatile("cp.async.wait_group %0;\n" ::"n"(kRowAhead) : "memory");
+          int64_t now[4];
 #pragma unroll
-          for (int u = 0; u < 4; ++u) now[u] = ahead[u];
-          if (r0 + R < seg_hi) fetch(r0 + R);
+          for (int u = 0; u < 4; ++u) {
+            const int i = lane + 32 * u;
+            now[u] = i < R ? ring[(m & 3) * 128 + i] : -1;
+          }
+          // validity, and whether row i continues row i - 1 in the pool within
+          // one group (so that one copy covers both)
+          int64_t src[4];
+          bool ok[4], cont[4];
           int nvalid = 0;
           uint32_t bits[4] = {0u, 0u, 0u, 0u};
 #pragma unroll
           for (int u = 0; u < 4; ++u) {
             const int64_t row = now[u];
-            blk[u] = 0;
-            off[u] = 0;
+            int64_t blk = 0, off = 0;
             if (row >= 0) {
               if (p.page_shift >= 0) {
-                blk[u] = row >> p.page_shift;
-                off[u] = row & (p.page_size - 1);
+                blk = row >> p.page_shift;
+                off = row & (p.page_size - 1);
               } else {
-                blk[u] = row / p.page_size;
-                off[u] = row % p.page_size;
+                blk = row / p.page_size;
+                off = row % p.page_size;
               }
             }
-            ok[u] = row >= 0 && blk[u] < p.pool_blocks;
+            ok[u] = row >= 0 && blk < p.pool_blocks;
             if (row >= 0 && !ok[u]) flag(p.status, HS_DEV_ROW_OUT_OF_RANGE);
-            src_off[u] = (blk[u] * 2 * p.page_size + off[u]) * row_bytes;
+            src[u] = ok[u] ? (blk * 2 * p.page_size + off) * row_bytes : 0;
             nvalid += ok[u];
-            const int j = lane + 32 * (u >> 1);
-            const int sl = (j >> 3) * 16 + (j & 7) + (u & 1) * 8;
+            // the previous tile row is the lane below's (G divides 32, so lane 0
+            // always opens a group and never continues a row)
+            const int64_t before = __shfl_up_sync(kFullMask, row, 1);
+            const int i = lane + 32 * u;
+            cont[u] = ok[u] && i % sh.run != 0 && before >= 0 && row == before + 1 &&
+                      off != 0;  // same block: the row does not open a block
+            const int sl = tile_slot(sh, i);
 #pragma unroll
             for (int wi = 0; wi < 4; ++wi)
               if (ok[u] && (sl >> 5) == wi) bits[wi] |= 1u << (sl & 31);
           }
           const int valid_total = warp_sum_int(nvalid);
           if (lane == 0) mbar_add_tx(&full[st], (unsigned)(valid_total * 2 * row_bytes));
-          __syncwarp();
+          // The stage's copies: every valid row that does not continue the row
+          // before it starts one K copy and one V copy as long as its run. They
+          // are dealt to the lanes through registers (copy c of a 32-row word:
+          // lane c % 32, start number c / 2): a thread's shared-memory loads
+          // would wait for the bulk copies it has in flight.
 #pragma unroll
-          for (int w = 0; w < 2; ++w) {
-            const int j = lane + 32 * w;
-            const int at = slot_offset(sh, (j >> 3) * 16 + (j & 7));  // its pair slot: + row_bytes
-            const int ua = 2 * w, ub = 2 * w + 1;
-            if (ok[ua] && ok[ub] && blk[ub] == blk[ua] && off[ub] == off[ua] + 1) {
-              // consecutive rows of one block: one copy of both K rows, one of both V rows
-              bulk_copy(kb + at, pool + src_off[ua], (unsigned)(2 * row_bytes), &full[st]);
-              bulk_copy(vb + at, pool + src_off[ua] + plane, (unsigned)(2 * row_bytes), &full[st]);
-            } else {
-              if (ok[ua]) {
-                bulk_copy(kb + at, pool + src_off[ua], (unsigned)row_bytes, &full[st]);
-                bulk_copy(vb + at, pool + src_off[ua] + plane, (unsigned)row_bytes, &full[st]);
-              }
-              if (ok[ub]) {
-                bulk_copy(kb + at + row_bytes, pool + src_off[ub], (unsigned)row_bytes,
-                          &full[st]);
-                bulk_copy(vb + at + row_bytes, pool + src_off[ub] + plane, (unsigned)row_bytes,
-                          &full[st]);
+          for (int u = 0; u < 4; ++u) {
+            if (32 * u >= R) break;
+            const uint32_t cont_w = __ballot_sync(kFullMask, cont[u]);
+            const unsigned starts = __ballot_sync(kFullMask, ok[u] && !cont[u]);
+            // rows continuing this one: the run of set bits of cont_w above the lane
+            const uint32_t above = lane < 31 ? cont_w >> (lane + 1) : 0u;
+            // 1 + trailing ones; a run never passes its group's end (kept as a bound)
+            const int len = min(__ffs(~above), sh.run - (lane + 32 * u) % sh.run);
+            const int dst = slot_offset(sh, tile_slot(sh, lane + 32 * u));
+            const int n_copies = 2 * __popc(starts);
+            for (int c0 = 0; c0 < n_copies; c0 += 32) {
+              const int c = c0 + lane;
+              const int from = c < n_copies ? (int)__fns(starts, 0, (c >> 1) + 1) : 0;
+              const int64_t c_src = __shfl_sync(kFullMask, src[u], from);
+              const int c_len = __shfl_sync(kFullMask, len, from);
+              const int c_dst = __shfl_sync(kFullMask, dst, from);
+              if (c < n_copies) {
+                const int v = c & 1;  // 0: K plane, 1: V plane
+                bulk_copy(kb + v * sh.plane_bytes + c_dst, pool + c_src + v * plane,
+                          (unsigned)(c_len * row_bytes), &full[st]);
               }
             }
           }
@@ -748,7 +796,7 @@ __global__ void __launch_bounds__(kBulkThreads, 1) attend_bulk_kernel(AttendPara
             while (bad) {
               const int sl = 32 * wi + __ffs(bad) - 1;
               bad &= bad - 1;
-              char *dst = vb + slot_offset(sh, sl);
+              char *dst = kb + sh.plane_bytes + slot_offset(sh, sl);
               for (int c = lane; c < sh.row_bytes / 16; c += 32)
                 *reinterpret_cast<uint4 *>(dst + c * 16) = make_uint4(0, 0, 0, 0);
             }
@@ -762,22 +810,21 @@ __global__ void __launch_bounds__(kBulkThreads, 1) attend_bulk_kernel(AttendPara
           __syncwarp();
           if (lane == 0) mbar_arrive(&full[st]);
         }
+        t += (int)seg_tiles;
       }
       start += chunk_total;
     }
-    // end record
-    if (alive) {
-      const int st = t % kBulkStages;
-      if (claim(st)) {
-        if (lane == 0) {
-          info[st].b = -1;
-          mbar_arrive(&full[st]);
-        }
-        ++t;
+    // end record, by the warp that owns stage t
+    if (alive && t % kBulkProducers == pw && claim(t)) {
+      if (lane == 0) {
+        info[t % kBulkStages].b = -1;
+        mbar_arrive(&full[t % kBulkStages]);
       }
     }
+    ++t;
     __syncwarp();
-    // no copy may still be landing when the CTA exits
+    asm volatile("cp.async.wait_group 0;\n" ::: "memory");
+    // no copy may still be landing when the CTA exits: the last stages' phases
     if (lane == 0)
       for (int u = max(0, t - kBulkStages); u < t; ++u)
         mbar_wait(&full[u % kBulkStages], (u / kBulkStages) & 1, p.status);
@@ -785,7 +832,7 @@ __global__ void __launch_bounds__(kBulkThreads, 1) attend_bulk_kernel(AttendPara
   }
 
   // ---------------- consumers ----------------
-  const int c = warp - 1;
+  const int c = warp - kBulkProducers;
   const int kh = c % p.kv_heads, sub = c / p.kv_heads;
   const int groups = p.q_heads / p.kv_heads;
   const int h0 = kh * groups;

@@ -123,7 +123,8 @@ class DecodeBatch:
 
     def layer(self, layer: int, query: torch.Tensor, out: torch.Tensor | None = None,
               counts: torch.Tensor | None = None, timing: list | None = None,
-              stages=None, serial: bool = False, part: str = "all") -> torch.Tensor:
+              stages=None, serial: bool = False, part: str = "all",
+              positions: torch.Tensor | None = None) -> torch.Tensor:
         """Hot path of `layer` for query [B, Hq, D] (CUDA, contiguous) on the
         cache's compute stream; returns attention output [B, Hq, D].
 
@@ -142,7 +143,12 @@ class DecodeBatch:
         (with a group) or the whole selection (without), "tail" everything
         after, and neither runs the all-gather: the caller issues it between
         them on the stream that orders the two (DecodeGraph's segmented
-        replay)."""
+        replay).
+
+        positions: optional int32 [B, width] CUDA tensor of logical token
+        positions (-1 padded, width = top_pages * page_size) to resolve in
+        place of the Quest selection, which is then skipped (an externally
+        chosen selection, e.g. a replayed trace)."""
         if part not in ("all", "head", "tail"):
             raise ValueError("part must be 'all', 'head' or 'tail'")
         cfg, st, compute = self.config, self.layers[layer], self.compute
@@ -165,6 +171,21 @@ class DecodeBatch:
             event.record(stream_)
             return event
 
+        if positions is not None:
+            if part != "all":
+                raise ValueError("positions replace the whole selection: part must be 'all'")
+            if (positions.shape != (b, self.width) or positions.dtype != torch.int32
+                    or positions.device != self.device or not positions.is_contiguous()):
+                raise ValueError("positions must be a contiguous int32 [batch, width] tensor "
+                                 "on the batch's device")
+            if st.ready is not None:
+                compute.wait_event(st.ready)
+            t1 = mark(compute, "resolve")
+            self._rest(layer, query, out, counts, timing, stages, serial, mark, None, t1,
+                       positions.data_ptr())
+            st.last_use = torch.cuda.Event()
+            st.last_use.record(compute)
+            return out
         t0 = None
         if part != "tail":
             t0 = self._select_head(layer, query, mark)
@@ -175,7 +196,8 @@ class DecodeBatch:
         if self.group is not None:
             self._select_tail(layer, query)
         t1 = mark(compute, "quest", "resolve") if part == "all" else mark(compute, "resolve")
-        self._rest(layer, query, out, counts, timing, stages, serial, mark, t0, t1)
+        self._rest(layer, query, out, counts, timing, stages, serial, mark, t0, t1,
+                   self.tokens.data_ptr())
         st.last_use = torch.cuda.Event()
         st.last_use.record(compute)
         return out
@@ -222,14 +244,14 @@ class DecodeBatch:
             _lib.ptr(self.quest_ws), self.quest_ws_bytes, self.status.data_ptr(),
             self.compute.cuda_stream))
 
-    def _rest(self, layer, query, out, counts, timing, stages, serial, mark, t0, t1):
+    def _rest(self, layer, query, out, counts, timing, stages, serial, mark, t0, t1, tokens):
         """Resolve, gather, both attention phases and the merge of `layer`."""
         cache, cfg, st, lib = self.cache, self.config, self.layers[layer], _lib.load()
         b, hq, d = query.shape
         compute, transfer = self.compute, self.transfer
         stream, status = compute.cuda_stream, self.status.data_ptr()
         _lib.check(lib.hs_resolve_rows_batched(
-            b, self.tokens.data_ptr(), self.width, st.src_ptrs.data_ptr(), st.res_ptrs.data_ptr(),
+            b, tokens, self.width, st.src_ptrs.data_ptr(), st.res_ptrs.data_ptr(),
             st.table_pages, st.hot_ptrs.data_ptr(), cache.hot_blocks, st.tag_ptrs.data_ptr(),
             st.lru_ptrs.data_ptr(), self.hot_rows, st.lengths.data_ptr(), cfg.page_size,
             self.physical.data_ptr(), self.miss_host.data_ptr(), self.miss_device.data_ptr(),

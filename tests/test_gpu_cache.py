@@ -165,6 +165,37 @@ def test_decode_batch_against_oracle_full_step():
     assert torch.equal(cache.pool.cpu(), pool_cpu)
 
 
+def test_decode_batch_with_external_positions_matches_quest_path():
+    """layer(positions=...) resolves a given selection instead of running Quest:
+    fed the tokens Quest chose, it leaves the same outputs, counts, tags and LRU
+    as the Quest path; bad shapes are rejected."""
+    b, length, p, hkv, d, hq, top = 3, 4000, 16, 8, 128, 32, 16
+    config, hot, host, placement, meta = _build(4, b, 1, length, p, hkv, d, 512, 0.25,
+                                                torch.bfloat16)
+    cache_a = _cache(config, hot, host, placement, length)
+    cache_b = _cache(config, hot, host, placement, length)
+    mins = {r: meta[r][0].to(DEV) for r in range(b)}
+    maxs = {r: meta[r][1].to(DEV) for r in range(b)}
+    batch_a = DecodeBatch(cache_a, list(range(b)), 1, mins, maxs, top, hq)
+    batch_b = DecodeBatch(cache_b, list(range(b)), 1, mins, maxs, top, hq)
+    gen = torch.Generator().manual_seed(5)
+    for step in range(3):
+        q = torch.randn(b, hq, d, generator=gen).to(torch.bfloat16).to(DEV)
+        out_a = batch_a.layer(0, q).clone()
+        tokens = batch_a.tokens.clone()
+        out_b = batch_b.layer(0, q, positions=tokens).clone()
+        assert torch.equal(out_a, out_b)
+        assert torch.equal(batch_a.last_counts(), batch_b.last_counts())
+        for r in range(b):
+            ta, tb = cache_a.tables[r, 0], cache_b.tables[r, 0]
+            assert torch.equal(ta.tags, tb.tags) and torch.equal(ta.lru, tb.lru)
+    with pytest.raises(ValueError, match="positions"):
+        batch_b.layer(0, q, positions=tokens[:, :-1].contiguous())
+    with pytest.raises(ValueError, match="positions"):
+        batch_b.layer(0, q, positions=tokens.long())
+    assert not _lib.device_flags(DEV)
+
+
 @pytest.mark.parametrize("segmented", [False, True])
 def test_decode_graph_replay_matches_eager_steps(segmented):
     """A whole step captured as a CUDA graph (two micro-batches on their own
