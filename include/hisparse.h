@@ -116,11 +116,14 @@ HS_API int hs_host_device_pointer(const void *host, void **device_alias);
  * -1 padding up to out_capacity (>= top_pages * page_size);
  * out_count receives the number of tokens.
  * The fp32 summation order is fixed, so scores are reproducible bit for bit:
- * with C = ceil(head_dim / 32), lane j in [0, 32) adds the terms
- * d = j*C .. j*C+C-1 (d < head_dim) left to right; the 32 lane sums are then
- * combined pairwise as (j, j^16), (j, j^8), (j, j^4), (j, j^2), (j, j^1).
- * The head sums are combined the same way (lane j adds heads j, j+32, ...
- * left to right, then the same xor tree) and divided by q_heads.
+ * with L = the smallest power of two >= ceil(head_dim / 8), lane j in [0, L)
+ * owns d = 8j .. 8j+7 (d < head_dim); it adds the terms at even offsets
+ * (d = 8j, 8j+2, ...) left to right and those at odd offsets left to right,
+ * then even + odd; the L lane values are combined pairwise as
+ * (j, j^(L/2)), (j, j^(L/4)), ..., (j, j^1). The head sums are then combined
+ * with 32 lanes: lane j adds heads j, j+32, ... left to right, the 32 lane
+ * values meet in the xor tree (j, j^16), ..., (j, j^1), and the total is
+ * divided by q_heads.
  */
 /* Workspace: per-request scores plus one completion counter per request. The
  * counters must be zero before the first use (zero-fill the whole workspace

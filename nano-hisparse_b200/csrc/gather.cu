@@ -33,6 +33,12 @@ struct GatherParams {
 // Two warps of at most 64 registers (4 K registers a CTA): the gather CTAs of
 // two micro-batches fit on an SM beside a Quest or attention CTA, so the
 // kernels that overlap the gather are not held back waiting for its registers.
+// The plan is scanned 32 entries per load (one per lane, kChunks chunks per
+// warp at once): most entries are -1 padding after each request's compact
+// prefix, and a warp that read them one at a time paid an L2 round trip per
+// entry (~0.3 ms for a 64 x 4096-entry plan with nothing to move).
+constexpr int kChunks = 2;
+
 template <typename V>
 __global__ void __launch_bounds__(kGatherThreads, 16) gather_kernel(GatherParams p) {
   const int lane = threadIdx.x & 31;
@@ -40,36 +46,53 @@ __global__ void __launch_bounds__(kGatherThreads, 16) gather_kernel(GatherParams
   const int64_t warps = (int64_t)gridDim.x * kGatherWarps;
   const int vecs = (int)(p.row_bytes / (int64_t)sizeof(V));  // per plane
   const int64_t plane_stride = (int64_t)p.page_size * p.row_bytes;
-  for (int64_t e = warp; e < p.count; e += warps) {
-    const int64_t h = p.miss_host[e], d = p.miss_device[e];
-    if (h < 0 || d < 0) continue;  // padding after the compact prefix
-    const int64_t hb = h / p.page_size, db = d / p.page_size;
-    if (hb >= p.host_blocks || db >= p.pool_blocks) {
-      if (lane == 0) flag(p.status, HS_DEV_ROW_OUT_OF_RANGE);
-      continue;
+  const int64_t chunks = ceil_div(p.count, (int64_t)32);
+  for (int64_t c0 = warp * kChunks; c0 < chunks; c0 += warps * kChunks) {
+    int64_t hs_[kChunks], ds_[kChunks];
+#pragma unroll
+    for (int k = 0; k < kChunks; ++k) {
+      const int64_t e = (c0 + k) * 32 + lane;
+      const bool in = c0 + k < chunks && e < p.count;
+      hs_[k] = in ? __ldcg(p.miss_host + e) : -1;
+      ds_[k] = in ? __ldcg(p.miss_device + e) : -1;
     }
-    const char *src = p.host + (hb * 2 * p.page_size + h % p.page_size) * p.row_bytes;
-    char *dst = p.pool + (db * 2 * p.page_size + d % p.page_size) * p.row_bytes;
-    const V *k_src = reinterpret_cast<const V *>(src);
-    const V *v_src = reinterpret_cast<const V *>(src + plane_stride);
-    V *k_dst = reinterpret_cast<V *>(dst);
-    V *v_dst = reinterpret_cast<V *>(dst + plane_stride);
-    for (int c0 = lane; c0 < vecs; c0 += 32 * kUnroll) {
-      V k[kUnroll], v[kUnroll];
 #pragma unroll
-      for (int u = 0; u < kUnroll; ++u) {
-        const int c = c0 + 32 * u;
-        if (c < vecs) {
-          k[u] = __ldcs(k_src + c);  // host rows are read once: stream past the caches
-          v[u] = __ldcs(v_src + c);
+    for (int k = 0; k < kChunks; ++k) {
+      unsigned todo = __ballot_sync(kFullMask, hs_[k] >= 0 && ds_[k] >= 0);
+      while (todo) {
+        const int j = __ffs(todo) - 1;
+        todo &= todo - 1;
+        const int64_t h = __shfl_sync(kFullMask, hs_[k], j);
+        const int64_t d = __shfl_sync(kFullMask, ds_[k], j);
+        const int64_t hb = h / p.page_size, db = d / p.page_size;
+        if (hb >= p.host_blocks || db >= p.pool_blocks) {
+          if (lane == 0) flag(p.status, HS_DEV_ROW_OUT_OF_RANGE);
+          continue;
         }
-      }
+        const char *src = p.host + (hb * 2 * p.page_size + h % p.page_size) * p.row_bytes;
+        char *dst = p.pool + (db * 2 * p.page_size + d % p.page_size) * p.row_bytes;
+        const V *k_src = reinterpret_cast<const V *>(src);
+        const V *v_src = reinterpret_cast<const V *>(src + plane_stride);
+        V *k_dst = reinterpret_cast<V *>(dst);
+        V *v_dst = reinterpret_cast<V *>(dst + plane_stride);
+        for (int c_ = lane; c_ < vecs; c_ += 32 * kUnroll) {
+          V kv[kUnroll], vv[kUnroll];
 #pragma unroll
-      for (int u = 0; u < kUnroll; ++u) {
-        const int c = c0 + 32 * u;
-        if (c < vecs) {
-          k_dst[c] = k[u];
-          v_dst[c] = v[u];
+          for (int u = 0; u < kUnroll; ++u) {
+            const int c = c_ + 32 * u;
+            if (c < vecs) {
+              kv[u] = __ldcs(k_src + c);  // host rows are read once: stream past the caches
+              vv[u] = __ldcs(v_src + c);
+            }
+          }
+#pragma unroll
+          for (int u = 0; u < kUnroll; ++u) {
+            const int c = c_ + 32 * u;
+            if (c < vecs) {
+              k_dst[c] = kv[u];
+              v_dst[c] = vv[u];
+            }
+          }
         }
       }
     }
@@ -96,7 +119,7 @@ extern "C" int hs_gather_rows(const void *host_alias, int64_t host_blocks, void 
                  device_status};
   const uintptr_t align = reinterpret_cast<uintptr_t>(host_alias) |
                           reinterpret_cast<uintptr_t>(pool) | (uintptr_t)row_bytes;
-  const int64_t warps_needed = count;
+  const int64_t warps_needed = ceil_div(ceil_div(count, (int64_t)32), (int64_t)kChunks);
   int64_t blocks = ceil_div(warps_needed, kGatherWarps);
   // One small CTA per SM at most: enough host-link reads in flight while leaving
   // each SM room for the kernels that overlap the gather.

@@ -6,24 +6,29 @@
 // (LogicalTopK.from_selection, shared case).
 //
 // Grid (ctas_per_request, batch). A CTA scores one tile of pages of one
-// request; its work items are (KV head, group of 4 query heads, 8 pages):
-// each lane owns C = ceil(D/32) consecutive head-dim elements, holds its
-// slice of q for the 4 heads in registers, streams the 8 pages' min/max
-// slices, and a 31-shuffle reduce-scatter leaves one (page, head) sum per
-// lane. Head sums meet in shared memory and are combined per page. The last
-// CTA of a request to finish (a completion counter in the workspace) runs the
-// top-k: an MSB-first radix select over order-preserving score keys, then the
-// chosen pages are scanned in page order so tokens come out sorted.
+// request; a warp serves one (KV head, group of 4 query heads) and scores
+// 32 / L pages at a time, L = the lanes sharing one page's row (L = 16 at
+// head_dim 128): each lane holds its 8 head-dim elements of q for the 4 heads,
+// widens 8 min and 8 max elements into packed pairs and runs 32 packed FMAs;
+// a 4-value lane reduction (two halving levels, then whole values) leaves one
+// (page, head) sum per lane group. Head sums meet in shared memory and are
+// combined per page. The last CTA of a request to finish (a completion counter
+// in the workspace) runs the top-k: an MSB-first radix select over
+// order-preserving score keys, then the chosen pages are scanned in page order
+// so tokens come out sorted.
 //
 // Fixed fp32 order (reproducible bit for bit; the oracle restates it):
-//   part[h, j]  = sum over d = j*C .. j*C+C-1 of max(q*min, q*max), left to right
-//   s[h]        = xor tree over lanes j of part[h, j]: pairs (j, j^16), (j^8), ..., (j^1)
+//   L           = smallest power of two >= ceil(D / 8)
+//   a[h, j]     = terms d = 8j, 8j+2, 8j+4, 8j+6 (d < D) of max(q*min, q*max),
+//                 left to right; b[h, j] the same at 8j+1, 8j+3, ...
+//   part[h, j]  = a + b
+//   s[h]        = xor tree over lanes j < L: pairs (j, j^(L/2)), ..., (j, j^1)
 //   u[j]        = sum over heads h = j, j+32, ... of s[h], left to right
-//   score       = (xor tree over j of u[j]) / q_heads
+//   score       = (xor tree over 32 lanes of u[j]) / q_heads
 // For 16-bit q and metadata, max(q*min, q*max) is evaluated as
 // fma(q+, max, .) then fma(q-, min, .) with q+ = max(q, 0), q- = min(q, 0):
 // the products of two 16-bit floats are exact in fp32 and min <= max, so the
-// sums are bit-identical and cost two FFMA per term instead of four ops.
+// sums are bit-identical and an (even, odd) pair of terms costs two packed FMAs.
 #include <cstdio>
 #include <mutex>
 
@@ -362,12 +367,121 @@ __device__ void select_request(const QuestParams<TQ, TKV> &p, int b, int64_t len
   if (tid == 0) p.out_counts[b] = (int32_t)count;
 }
 
+// ---- the per-lane arithmetic of the fixed order ------------------------------
+// Lane j of the L lanes that share a (page, KV head) row owns elements
+// d = 8j .. 8j+7. For each of up to 4 query heads it adds the terms
+// max(q*min, q*max) at even offsets left to right and those at odd offsets
+// left to right, then even + odd; lane_reduce4 combines the L lanes by the xor
+// tree. L = the smallest power of two >= ceil(head_dim / 8).
+constexpr int kMaxQuestLanes = 32;
+
+__host__ __device__ inline int quest_lanes(int head_dim) {
+  int L = 1;
+  while (L * 8 < head_dim) L *= 2;
+  return L;
+}
+
+// Two packed 16-bit elements (element 2k in the low half) widened to fp32.
+template <typename T> __device__ __forceinline__ float2 pair_f32(uint32_t w);
+template <> __device__ __forceinline__ float2 pair_f32<__nv_bfloat16>(uint32_t w) {
+  return make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xffff0000u));
+}
+template <> __device__ __forceinline__ float2 pair_f32<__half>(uint32_t w) {
+  __half2 h;
+  *reinterpret_cast<uint32_t *>(&h) = w;
+  return __half22float2(h);
+}
+
+// 16-bit q and metadata: q+ = max(q, 0) and q- = min(q, 0) as packed pairs
+// (qa, qb: [head][pair]); one packed FMA serves the even and the odd term of a
+// pair. max(q*min, q*max) = q+*max + q-*min exactly (products of 16-bit floats
+// are exact in fp32, min <= max, one of q+ / q- is zero), so each term is one
+// rounding of acc + term.
+template <typename TKV>
+__device__ __forceinline__ void score16(const uint4 &mn, const uint4 &mx, const float2 (&qa)[4][4],
+                                        const float2 (&qb)[4][4], float (&v)[4]) {
+  float2 acc[4];
+#pragma unroll
+  for (int h = 0; h < 4; ++h) acc[h] = make_float2(0.f, 0.f);
+  const uint32_t lw[4] = {mn.x, mn.y, mn.z, mn.w}, hw[4] = {mx.x, mx.y, mx.z, mx.w};
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const float2 hi = pair_f32<TKV>(hw[k]), lo = pair_f32<TKV>(lw[k]);
+#pragma unroll
+    for (int h = 0; h < 4; ++h) {
+      acc[h] = __ffma2_rn(qa[h][k], hi, acc[h]);
+      acc[h] = __ffma2_rn(qb[h][k], lo, acc[h]);
+    }
+  }
+#pragma unroll
+  for (int h = 0; h < 4; ++h) v[h] = __fadd_rn(acc[h].x, acc[h].y);
+}
+
+// Any other types: the terms computed and added one by one; `ne` of the 8
+// elements exist (head_dim - 8j, clamped to [0, 8]).
+__device__ __forceinline__ void score_f32(const float (&lo)[8], const float (&hi)[8], int ne,
+                                          const float (&q)[4][8], float (&v)[4]) {
+#pragma unroll
+  for (int h = 0; h < 4; ++h) {
+    float a = 0.f, b = 0.f;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      if (e < ne) {
+        const float t = fmaxf(__fmul_rn(q[h][e], lo[e]), __fmul_rn(q[h][e], hi[e]));
+        if (e & 1) b = e == 1 ? t : __fadd_rn(b, t);
+        else a = e == 0 ? t : __fadd_rn(a, t);
+      }
+    }
+    v[h] = ne > 1 ? __fadd_rn(a, b) : (ne == 1 ? a : 0.f);
+  }
+}
+
+// Xor tree over the L lanes of a group for 4 values at once: the first two
+// levels halve the values each lane keeps (recursive halving), the rest add
+// whole values. Afterwards the lane holds kValues head sums, heads
+// hbase .. hbase + kValues - 1; `writer` marks one lane per group and head.
+template <int L> struct LaneReduce {
+  static constexpr int kValues = L >= 4 ? 1 : (L == 2 ? 2 : 4);
+  float out[kValues];
+  int hbase;
+  bool writer;
+  __device__ __forceinline__ LaneReduce(const float (&v)[4], int lane) {
+    float w[4] = {v[0], v[1], v[2], v[3]};
+    hbase = 0;
+    if constexpr (L >= 2) {
+      constexpr int o = L / 2;
+      const bool up = (lane & o) != 0;
+      const float s0 = up ? w[0] : w[2], s1 = up ? w[1] : w[3];
+      const float k0 = up ? w[2] : w[0], k1 = up ? w[3] : w[1];
+      w[0] = __fadd_rn(k0, __shfl_xor_sync(kFullMask, s0, o));
+      w[1] = __fadd_rn(k1, __shfl_xor_sync(kFullMask, s1, o));
+      hbase = up ? 2 : 0;
+    }
+    if constexpr (L >= 4) {
+      constexpr int o = L / 4;
+      const bool up = (lane & o) != 0;
+      const float sd = up ? w[0] : w[1], kp = up ? w[1] : w[0];
+      w[0] = __fadd_rn(kp, __shfl_xor_sync(kFullMask, sd, o));
+      hbase += up ? 1 : 0;
+#pragma unroll
+      for (int o2 = L / 8; o2 > 0; o2 >>= 1) w[0] = __fadd_rn(w[0], __shfl_xor_sync(kFullMask, w[0], o2));
+      writer = (lane & (L / 4 - 1)) == 0;
+    } else {
+      writer = true;
+    }
+#pragma unroll
+    for (int i = 0; i < kValues; ++i) out[i] = w[i];
+  }
+};
+
 // ---- scoring ------------------------------------------------------------------------
-template <typename TQ, typename TKV, int C>
+template <typename TQ, typename TKV, int L>
 __global__ void __launch_bounds__(kThreads, 2) quest_kernel(QuestParams<TQ, TKV> p) {
   extern __shared__ float head_sums[];  // [tile_pages][q_heads]
   __shared__ int s_last;
   constexpr bool kFma = is16<TQ>() && is16<TKV>();
+  constexpr int kPass = 32 / L;   // pages a warp scores at once
+  constexpr int kUnroll = 4;      // passes whose loads are in flight together
   const int b = blockIdx.y;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int64_t length = p.lengths.at(b);
@@ -379,79 +493,81 @@ __global__ void __launch_bounds__(kThreads, 2) quest_kernel(QuestParams<TQ, TKV>
     const int64_t tile_n = min((int64_t)p.tile_pages, n - tile0);
     const int groups = Hq / p.kv_heads;
     const int chunks = (groups + kHeadsPerItem - 1) / kHeadsPerItem;
-    const int page_groups = (int)ceil_div(tile_n, kPagesPerItem);
+    const int passes = (int)ceil_div(tile_n, (int64_t)kPass);
     const TQ *q = p.query.at(b);
     const TKV *mn_base = p.minimum.at(b);
     const TKV *mx_base = p.maximum.at(b);
-    const int d0 = lane * C;
+    const int pl = lane / L, j = lane % L, d0 = 8 * j;
+    const int ne = D - d0 < 0 ? 0 : (D - d0 > 8 ? 8 : D - d0);
+    const bool vec = ne == 8 && sizeof(TKV) == 2 && (D % 8) == 0 &&
+                     ((reinterpret_cast<uintptr_t>(mn_base) | reinterpret_cast<uintptr_t>(mx_base)) & 15) == 0;
     // Each warp keeps one (KV head, head chunk) and its q slice in registers
-    // while it walks the tile's page groups.
+    // while it walks the tile's pages, kPass pages per pass.
     for (int khc = warp; khc < p.kv_heads * chunks; khc += kWarps) {
       const int hc = khc % chunks, kh = khc / chunks;
       const int h_begin = kh * groups + hc * kHeadsPerItem;
       const int h_count = min(kHeadsPerItem, kh * groups + groups - h_begin);
-      float qa[kHeadsPerItem][C], qb[kHeadsPerItem][C];
+      float qf[4][8];
 #pragma unroll
-      for (int g = 0; g < kHeadsPerItem; ++g)
+      for (int h = 0; h < 4; ++h)
 #pragma unroll
-        for (int c = 0; c < C; ++c) {
-          const float v = (g < h_count && d0 + c < D)
-                              ? to_f32(q[(int64_t)(h_begin + g) * D + d0 + c]) : 0.f;
-          qa[g][c] = kFma ? fmaxf(v, 0.f) : v;  // q+ (or q for the exact path)
-          qb[g][c] = kFma ? fminf(v, 0.f) : v;  // q-
+        for (int e = 0; e < 8; ++e)
+          qf[h][e] = (h < h_count && e < ne) ? to_f32(q[(int64_t)(h_begin + h) * D + d0 + e]) : 0.f;
+      float2 qa[4][4], qb[4][4];
+#pragma unroll
+      for (int h = 0; h < 4; ++h)
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          qa[h][k] = make_float2(fmaxf(qf[h][2 * k], 0.f), fmaxf(qf[h][2 * k + 1], 0.f));
+          qb[h][k] = make_float2(fminf(qf[h][2 * k], 0.f), fminf(qf[h][2 * k + 1], 0.f));
         }
-      for (int pgi = 0; pgi < page_groups; ++pgi) {
-        // the 8 pages' raw min/max slices, all loads issued before any use
-        Raw<TKV, C> lo[kPagesPerItem], hi[kPagesPerItem];
-        const int64_t page0 = tile0 + (int64_t)pgi * kPagesPerItem;
+      for (int ps0 = 0; ps0 < passes; ps0 += kUnroll) {
+        // kUnroll passes' min/max slices, every load issued before any use
+        uint4 lo_w[kUnroll], hi_w[kUnroll];
+        float lo_f[kUnroll][8], hi_f[kUnroll][8];
 #pragma unroll
-        for (int i = 0; i < kPagesPerItem; ++i) {
-          const int64_t page = page0 + i;
-          const bool in = page < tile0 + tile_n;
-          const int64_t off = (page * p.kv_heads + kh) * D + d0;
-          lo[i].load(mn_base + off, in, d0, D);
-          hi[i].load(mx_base + off, in, d0, D);
-        }
-        // v[i*4 + g]: this lane's part for (page i, head g)
-        float v[32];
+        for (int u = 0; u < kUnroll; ++u) {
+          const int64_t lp = (int64_t)(ps0 + u) * kPass + pl;
+          const bool in = ps0 + u < passes && lp < tile_n;
+          const int64_t off = ((tile0 + lp) * p.kv_heads + kh) * D + d0;
+          if constexpr (kFma) {
+            if (vec) {
+              lo_w[u] = in ? __ldg(reinterpret_cast<const uint4 *>(mn_base + off)) : make_uint4(0, 0, 0, 0);
+              hi_w[u] = in ? __ldg(reinterpret_cast<const uint4 *>(mx_base + off)) : make_uint4(0, 0, 0, 0);
+            } else {
+              uint16_t lw[8], hw[8];
 #pragma unroll
-        for (int i = 0; i < kPagesPerItem; ++i) {
-          float l[C], h[C];
-          lo[i].unpack(l);
-          hi[i].unpack(h);
-#pragma unroll
-          for (int g = 0; g < kHeadsPerItem; ++g) {
-            float part = 0.f;
-#pragma unroll
-            for (int c = 0; c < C; ++c) {
-              if (d0 + c < D) {
-                if constexpr (kFma) {
-                  part = __fmaf_rn(qa[g][c], h[c], c == 0 ? 0.f : part);
-                  part = __fmaf_rn(qb[g][c], l[c], part);
-                } else {
-                  const float t = fmaxf(__fmul_rn(qa[g][c], l[c]), __fmul_rn(qa[g][c], h[c]));
-                  part = c == 0 ? t : __fadd_rn(part, t);
-                }
+              for (int e = 0; e < 8; ++e) {
+                lw[e] = (in && e < ne) ? reinterpret_cast<const uint16_t *>(mn_base)[off + e] : 0;
+                hw[e] = (in && e < ne) ? reinterpret_cast<const uint16_t *>(mx_base)[off + e] : 0;
               }
+              lo_w[u] = make_uint4(lw[0] | (uint32_t)lw[1] << 16, lw[2] | (uint32_t)lw[3] << 16,
+                                   lw[4] | (uint32_t)lw[5] << 16, lw[6] | (uint32_t)lw[7] << 16);
+              hi_w[u] = make_uint4(hw[0] | (uint32_t)hw[1] << 16, hw[2] | (uint32_t)hw[3] << 16,
+                                   hw[4] | (uint32_t)hw[5] << 16, hw[6] | (uint32_t)hw[7] << 16);
             }
-            v[i * kHeadsPerItem + g] = part;
+          } else {
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+              lo_f[u][e] = (in && e < ne) ? to_f32(mn_base[off + e]) : 0.f;
+              hi_f[u][e] = (in && e < ne) ? to_f32(mx_base[off + e]) : 0.f;
+            }
           }
         }
-        // reduce-scatter: after the step with offset o, v[0..o) hold the values
-        // whose index bits in [o, 32) equal the lane's; lane L ends with value L
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-          const bool upper = (lane & o) != 0;
+        for (int u = 0; u < kUnroll; ++u) {
+          if (ps0 + u >= passes) break;  // warp-uniform
+          float v[4];
+          if constexpr (kFma) score16<TKV>(lo_w[u], hi_w[u], qa, qb, v);
+          else score_f32(lo_f[u], hi_f[u], ne, qf, v);
+          const LaneReduce<L> r(v, lane);
+          const int64_t lp = (int64_t)(ps0 + u) * kPass + pl;
 #pragma unroll
-          for (int i = 0; i < o; ++i) {
-            const float send = upper ? v[i] : v[i + o];
-            const float keep = upper ? v[i + o] : v[i];
-            v[i] = __fadd_rn(keep, __shfl_xor_sync(kFullMask, send, o));
+          for (int i = 0; i < LaneReduce<L>::kValues; ++i) {
+            const int h = r.hbase + i;
+            if (r.writer && h < h_count && lp < tile_n) head_sums[lp * Hq + h_begin + h] = r.out[i];
           }
         }
-        const int i_page = lane / kHeadsPerItem, g = lane % kHeadsPerItem;
-        const int64_t local_page = (int64_t)pgi * kPagesPerItem + i_page;
-        if (g < h_count && local_page < tile_n) head_sums[local_page * Hq + h_begin + g] = v[0];
       }
     }
     __syncthreads();
@@ -492,7 +608,7 @@ constexpr int kTmaThreads = 512;
 constexpr int kTmaWarps = kTmaThreads / 32;
 constexpr int kTmaStagePages = 16;
 constexpr int kTmaStages = 3;
-template <typename TQ, typename TKV, int C>
+template <typename TQ, typename TKV, int D>
 __global__ void __launch_bounds__(kTmaThreads, 1) quest_tma_kernel(QuestParams<TQ, TKV> p) {
   extern __shared__ __align__(128) char smem[];
   __shared__ __align__(8) uint64_t full[kTmaStages];
@@ -503,7 +619,6 @@ __global__ void __launch_bounds__(kTmaThreads, 1) quest_tma_kernel(QuestParams<T
   const int64_t n = length > 0 ? ceil_div(length, p.page_size) : 0;
   const bool score = length > 0 && n <= p.max_pages && p.top_pages < n;
   const int64_t tile0 = (int64_t)blockIdx.x * p.tile_pages;
-  constexpr int D = 32 * C;  // the staged path requires head_dim == 32 * C
   const int Hq = p.q_heads, Hkv = p.kv_heads;
   const int64_t page_elems = (int64_t)Hkv * D;
   const unsigned page_bytes = (unsigned)(page_elems * sizeof(TKV));
@@ -540,16 +655,19 @@ __global__ void __launch_bounds__(kTmaThreads, 1) quest_tma_kernel(QuestParams<T
 
     const int groups = Hq / Hkv;
     const int chunks = (groups + kHeadsPerItem - 1) / kHeadsPerItem;
-    constexpr int kGroupsPerStage = kTmaStagePages / kPagesPerItem;  // 2
-    const int items = Hkv * chunks * kGroupsPerStage;
+    constexpr int L = D / 8;                            // lanes per page row (4, 8 or 16)
+    constexpr int kPass = 32 / L;                       // pages per warp pass
+    constexpr int kPassesPerStage = kTmaStagePages / kPass;
+    const int roles = Hkv * chunks;
+    const int items = roles * kPassesPerStage;
     const TQ *q = p.query.at(b);
-    const int d0 = lane * C;
-    constexpr bool kFma = is16<TQ>() && is16<TKV>();
-    int cur = -1;
-    // 16-bit data: q+ and q- held as duplicated pairs, the packed FMA's first
-    // operand for two pages at once (hoisted: a warp keeps its item's heads)
-    float2 qa2[kHeadsPerItem][C], qb2[kHeadsPerItem][C];
-    float qa[kHeadsPerItem][C], qb[kHeadsPerItem][C];
+    const int pl = lane / L, d0 = 8 * (lane % L);
+    const int role0 = warp % roles, pass0 = warp / roles;
+    const int role_step = kTmaWarps % roles, pass_step = kTmaWarps / roles;
+    int cur = -1, hc = 0, kh = 0, h_begin = 0, h_count = 0;
+    // q+ and q- of the item's 4 heads as packed (even, odd) pairs, loaded when
+    // the warp's (KV head, head chunk) changes
+    float2 qa[4][4], qb[4][4];
     for (int g = 0; g < nstages; ++g) {
       const int64_t pages = min((int64_t)kTmaStagePages, tile_n - (int64_t)g * kTmaStagePages);
       const char *buf = smem + (g % kTmaStages) * stage_bytes;
@@ -558,95 +676,51 @@ __global__ void __launch_bounds__(kTmaThreads, 1) quest_tma_kernel(QuestParams<T
       float *stage_sums = sums + (g & 1) * kTmaStagePages * Hq;
       const bool ready = mbar_wait(&full[g % kTmaStages], (g / kTmaStages) & 1, p.status);
       if (!ready) s_ok = 0;
+      // item = pass * roles + role: with roles dividing the warp count a warp
+      // keeps one role (and its q registers) for the whole tile. role and pass
+      // advance incrementally (no division per item).
+      int role = role0, pass = pass0;
       for (int item = warp; ready && item < items; item += kTmaWarps) {
-        const int pgi = item % kGroupsPerStage;
-        const int khc = item / kGroupsPerStage;
-        const int hc = khc % chunks, kh = khc / chunks;
-        const int h_begin = kh * groups + hc * kHeadsPerItem;
-        const int h_count = min(kHeadsPerItem, kh * groups + groups - h_begin);
-        if (khc != cur) {
-          cur = khc;
+        if (role != cur) {
+          cur = role;
+          hc = role % chunks;
+          kh = role / chunks;
+          h_begin = kh * groups + hc * kHeadsPerItem;
+          h_count = min(kHeadsPerItem, kh * groups + groups - h_begin);
 #pragma unroll
-          for (int hh = 0; hh < kHeadsPerItem; ++hh)
+          for (int h = 0; h < 4; ++h)
 #pragma unroll
-            for (int c = 0; c < C; ++c) {
-              const float v = hh < h_count ? to_f32(q[(int64_t)(h_begin + hh) * D + d0 + c]) : 0.f;
-              if constexpr (kFma) {
-                qa2[hh][c] = make_float2(fmaxf(v, 0.f), fmaxf(v, 0.f));
-                qb2[hh][c] = make_float2(fminf(v, 0.f), fminf(v, 0.f));
-              } else {
-                qa[hh][c] = v;
-                qb[hh][c] = v;
+            for (int k = 0; k < 4; ++k) {
+              float x0 = 0.f, x1 = 0.f;
+              if (h < h_count) {
+                x0 = to_f32(q[(int64_t)(h_begin + h) * D + d0 + 2 * k]);
+                x1 = to_f32(q[(int64_t)(h_begin + h) * D + d0 + 2 * k + 1]);
               }
+              qa[h][k] = make_float2(fmaxf(x0, 0.f), fmaxf(x1, 0.f));
+              qb[h][k] = make_float2(fminf(x0, 0.f), fminf(x1, 0.f));
             }
         }
-        float v[32];
-#pragma unroll
-        for (int i = 0; i < kPagesPerItem; i += 2) {
-          // pages i and i+1 side by side: one packed fp32x2 FMA serves both.
-          // Rows past the tile's last page hold stale data; their sums are
-          // never stored (lp < pages below), so the loads need no predicate.
-          const int lp = pgi * kPagesPerItem + i;
-          Raw<TKV, C> rl0, rh0, rl1, rh1;
-          rl0.load_shared_full(lo_s + lp * (int)page_elems + kh * D + d0, true);
-          rh0.load_shared_full(hi_s + lp * (int)page_elems + kh * D + d0, true);
-          rl1.load_shared_full(lo_s + (lp + 1) * (int)page_elems + kh * D + d0, true);
-          rh1.load_shared_full(hi_s + (lp + 1) * (int)page_elems + kh * D + d0, true);
-          if constexpr (kFma) {
-            float2 part[kHeadsPerItem];
-#pragma unroll
-            for (int c = 0; c < C; ++c) {
-              // the two pages' element c, widened straight into a packed pair
-              const float2 hi2 = make_float2(to_f32(rh0.e[c]), to_f32(rh1.e[c]));
-              const float2 lo2 = make_float2(to_f32(rl0.e[c]), to_f32(rl1.e[c]));
-#pragma unroll
-              for (int hh = 0; hh < kHeadsPerItem; ++hh) {
-                part[hh] = __ffma2_rn(qa2[hh][c], hi2, c == 0 ? make_float2(0.f, 0.f) : part[hh]);
-                part[hh] = __ffma2_rn(qb2[hh][c], lo2, part[hh]);
-              }
-            }
-#pragma unroll
-            for (int hh = 0; hh < kHeadsPerItem; ++hh) {
-              v[i * kHeadsPerItem + hh] = part[hh].x;
-              v[(i + 1) * kHeadsPerItem + hh] = part[hh].y;
-            }
-          } else {
-            float l0[C], h0[C], l1[C], h1[C];
-            rl0.unpack(l0);
-            rh0.unpack(h0);
-            rl1.unpack(l1);
-            rh1.unpack(h1);
-#pragma unroll
-            for (int hh = 0; hh < kHeadsPerItem; ++hh) {
-              float p0 = 0.f, p1 = 0.f;
-#pragma unroll
-              for (int c = 0; c < C; ++c) {
-                const float t0 = fmaxf(__fmul_rn(qa[hh][c], l0[c]), __fmul_rn(qa[hh][c], h0[c]));
-                const float t1 = fmaxf(__fmul_rn(qa[hh][c], l1[c]), __fmul_rn(qa[hh][c], h1[c]));
-                p0 = c == 0 ? t0 : __fadd_rn(p0, t0);
-                p1 = c == 0 ? t1 : __fadd_rn(p1, t1);
-              }
-              v[i * kHeadsPerItem + hh] = p0;
-              v[(i + 1) * kHeadsPerItem + hh] = p1;
-            }
-          }
+        // Pages past the tile's last page hold stale data; their sums are
+        // never stored (lp < pages below), so the loads need no predicate.
+        const int lp = pass * kPass + pl;
+        const int off = lp * (int)page_elems + kh * D + d0;
+        const uint4 lo = *reinterpret_cast<const uint4 *>(lo_s + off);
+        const uint4 hi = *reinterpret_cast<const uint4 *>(hi_s + off);
+        float v[4];
+        score16<TKV>(lo, hi, qa, qb, v);
+        const LaneReduce<L> r(v, lane);
+        if (r.writer && r.hbase < h_count && lp < pages)
+          stage_sums[lp * Hq + h_begin + r.hbase] = r.out[0];
+        role += role_step;
+        pass += pass_step;
+        if (role >= roles) {
+          role -= roles;
+          ++pass;
         }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-          const bool upper = (lane & o) != 0;
-#pragma unroll
-          for (int i = 0; i < o; ++i) {
-            const float send = upper ? v[i] : v[i + o];
-            const float keep = upper ? v[i + o] : v[i];
-            v[i] = __fadd_rn(keep, __shfl_xor_sync(kFullMask, send, o));
-          }
-        }
-        const int i_page = lane / kHeadsPerItem, hh = lane % kHeadsPerItem;
-        const int lp = pgi * kPagesPerItem + i_page;
-        if (hh < h_count && lp < pages) stage_sums[lp * Hq + h_begin + hh] = v[0];
       }
       __syncthreads();  // buffer g % kTmaStages consumed; stage sums complete
       if (tid == 0 && s_ok && g + kTmaStages < nstages) issue(g + kTmaStages);
+      // per page: lane j adds heads j, j+32, ... then the xor tree; divide by q_heads
       for (int lp = warp; lp < pages; lp += kTmaWarps) {
         float u = 0.f;
         for (int h = lane; h < Hq; h += 32) u = __fadd_rn(u, stage_sums[lp * Hq + h]);
@@ -1042,7 +1116,7 @@ int tile_pages_for(int batch, int64_t max_pages) {
 }
 
 template <typename TQ, typename TKV>
-int launch_tma(QuestParams<TQ, TKV> &p, int C, cudaStream_t stream) {
+int launch_tma(QuestParams<TQ, TKV> &p, cudaStream_t stream) {
   const size_t page_bytes = (size_t)p.kv_heads * p.head_dim * sizeof(TKV);
   const size_t smem = kTmaStages * 2 * kTmaStagePages * page_bytes +
                       2 * kTmaStagePages * (size_t)p.q_heads * sizeof(float);
@@ -1052,18 +1126,18 @@ int launch_tma(QuestParams<TQ, TKV> &p, int C, cudaStream_t stream) {
   tile = ceil_div(tile, kTmaStagePages) * kTmaStagePages;
   p.tile_pages = (int)tile;
   dim3 grid((unsigned)ceil_div(p.max_pages, tile), (unsigned)p.batch);
-#define HS_QUEST_TMA(CC)                                                                  \
-  case CC: {                                                                              \
-    auto k = quest_tma_kernel<TQ, TKV, CC>;                                               \
+#define HS_QUEST_TMA(DD)                                                                  \
+  case DD: {                                                                              \
+    auto k = quest_tma_kernel<TQ, TKV, DD>;                                               \
     const int rc = reserve_smem((const void *)k, smem, "quest");                          \
     if (rc != HS_OK) return rc;                                                           \
     k<<<grid, kTmaThreads, smem, stream>>>(p);                                            \
     break;                                                                                \
   }
-  switch (C) {
-    HS_QUEST_TMA(1)
-    HS_QUEST_TMA(2)
-    HS_QUEST_TMA(4)
+  switch (p.head_dim) {
+    HS_QUEST_TMA(32)
+    HS_QUEST_TMA(64)
+    HS_QUEST_TMA(128)
     default:
       return set_error(HS_ERR_UNSUPPORTED, "quest: no staged path for head_dim %d", p.head_dim);
   }
@@ -1071,48 +1145,49 @@ int launch_tma(QuestParams<TQ, TKV> &p, int C, cudaStream_t stream) {
   return check_launch("quest_tma_kernel");
 }
 
-// The staged path needs whole 16-byte page rows, 16-byte aligned metadata and
-// a ring that fits shared memory; other shapes use quest_kernel.
+// The staged path needs 16-bit data, head_dim 32, 64 or 128 (whole 16-byte
+// lane slices), 16-byte aligned metadata and a ring that fits shared memory;
+// other shapes use quest_kernel.
 template <typename TQ, typename TKV>
 bool tma_eligible(const QuestParams<TQ, TKV> &p, bool aligned) {
-  const int C = (p.head_dim + 31) / 32;
   const size_t page_bytes = (size_t)p.kv_heads * p.head_dim * sizeof(TKV);
   const size_t smem = kTmaStages * 2 * kTmaStagePages * page_bytes +
                       2 * kTmaStagePages * (size_t)p.q_heads * sizeof(float);
-  return aligned && page_bytes % 16 == 0 && smem <= 200 * 1024 && (C == 1 || C == 2 || C == 4) &&
-         p.head_dim % C == 0 && p.head_dim == 32 * C;
+  return is16<TQ>() && is16<TKV>() && aligned && page_bytes % 16 == 0 &&
+         smem <= 200 * 1024 && (p.head_dim == 32 || p.head_dim == 64 || p.head_dim == 128);
 }
 
 template <typename TQ, typename TKV>
 int launch(QuestParams<TQ, TKV> &p, cudaStream_t stream, bool aligned) {
-  const int C = (p.head_dim + 31) / 32;
-  if (tma_eligible(p, aligned)) return launch_tma(p, C, stream);
+  if constexpr (is16<TQ>() && is16<TKV>()) {
+    if (tma_eligible(p, aligned)) return launch_tma(p, stream);
+  }
   p.tile_pages = tile_pages_for(p.batch, p.max_pages);
   const size_t sums_bytes = (size_t)p.tile_pages * p.q_heads * sizeof(float);
   const size_t keys_bytes =
       (size_t)(p.max_pages < kSmemKeys ? p.max_pages : kSmemKeys) * sizeof(uint32_t);
   const size_t smem = sums_bytes > keys_bytes ? sums_bytes : keys_bytes;
   dim3 grid((unsigned)ceil_div(p.max_pages, p.tile_pages), (unsigned)p.batch);
-#define HS_QUEST_CASE(CC)                                                                 \
-  case CC: {                                                                              \
-    auto k = quest_kernel<TQ, TKV, CC>;                                                   \
+#define HS_QUEST_CASE(LL)                                                                 \
+  case LL: {                                                                              \
+    auto k = quest_kernel<TQ, TKV, LL>;                                                   \
     const int rc = reserve_smem((const void *)k, smem, "quest");                          \
     if (rc != HS_OK) return rc;                                                           \
     k<<<grid, kThreads, smem, stream>>>(p);                                               \
     break;                                                                                \
   }
-  switch (C) {
+  if (p.head_dim > 8 * kMaxQuestLanes)
+    return set_error(HS_ERR_UNSUPPORTED, "quest: head_dim %d > 256 is not supported",
+                     p.head_dim);
+  switch (quest_lanes(p.head_dim)) {
     HS_QUEST_CASE(1)
     HS_QUEST_CASE(2)
-    HS_QUEST_CASE(3)
     HS_QUEST_CASE(4)
-    HS_QUEST_CASE(5)
-    HS_QUEST_CASE(6)
-    HS_QUEST_CASE(7)
     HS_QUEST_CASE(8)
+    HS_QUEST_CASE(16)
+    HS_QUEST_CASE(32)
     default:
-      return set_error(HS_ERR_UNSUPPORTED, "quest: head_dim %d > 256 is not supported",
-                       p.head_dim);
+      return set_error(HS_ERR_UNSUPPORTED, "quest: head_dim %d is not supported", p.head_dim);
   }
 #undef HS_QUEST_CASE
   return check_launch("quest_kernel");

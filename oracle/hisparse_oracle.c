@@ -83,13 +83,33 @@ static float xor_tree32(float x[32]) {
 }
 
 /* ---- (1) Quest scores --------------------------------------------------- */
+/* Lanes that share one head's row: the smallest power of two >= ceil(D / 8). */
+static int quest_lanes(int D) {
+  int L = 1;
+  while (L * 8 < D) L *= 2;
+  return L;
+}
+
+/* xor-pairing tree over L (a power of two) values: (j, j^(L/2)), ..., (j, j^1). */
+static float xor_tree(float *x, int L) {
+  float y[32];
+  for (int o = L / 2; o > 0; o >>= 1) {
+    for (int j = 0; j < L; ++j) y[j] = x[j] + x[j ^ o];
+    memcpy(x, y, sizeof(float) * (size_t)L);
+  }
+  return x[0];
+}
+
 /* q: [Hq, D] (qdtype); mn/mx: [>= n, Hkv, D] (kvdtype); scores: [n].
  * divide = 0 leaves the head sum undivided: the partial score of one shard of a
- * head-sharded selection (heads indexed locally, same order). */
+ * head-sharded selection (heads indexed locally, same order).
+ * Order (include/hisparse.h states it): lane j of L owns d = 8j .. 8j+7; it
+ * adds the terms at even offsets left to right and those at odd offsets left
+ * to right, then even + odd; the L lane values meet in the xor tree. */
 static int quest_scores(const void *q, int qdtype, const void *mn, const void *mx, int kvdtype,
                         int Hq, int Hkv, int D, int64_t n, float *scores, int divide) {
-  if (Hq < 1 || Hkv < 1 || D < 1 || Hq % Hkv) return 1;
-  const int g = Hq / Hkv, C = (D + 31) / 32;
+  if (Hq < 1 || Hkv < 1 || D < 1 || D > 256 || Hq % Hkv) return 1;
+  const int g = Hq / Hkv, L = quest_lanes(D);
   float *qf = (float *)malloc(sizeof(float) * (size_t)Hq * D);
   float *s = (float *)malloc(sizeof(float) * (size_t)Hq);
   float *lo = (float *)malloc(sizeof(float) * (size_t)D);
@@ -97,7 +117,6 @@ static int quest_scores(const void *q, int qdtype, const void *mn, const void *m
   if (!qf || !s || !lo || !hi) return 2;
   for (int64_t i = 0; i < (int64_t)Hq * D; ++i) qf[i] = load_elem(q, qdtype, i);
   for (int64_t p = 0; p < n; ++p) {
-    /* s[h]: lane j adds its C terms left to right, lanes meet in the xor tree */
     for (int kh = 0; kh < Hkv; ++kh) {
       const int64_t row = (p * Hkv + kh) * (int64_t)D;
       for (int d = 0; d < D; ++d) {
@@ -106,20 +125,20 @@ static int quest_scores(const void *q, int qdtype, const void *mn, const void *m
       }
       for (int h = kh * g; h < kh * g + g; ++h) {
         float part[32];
-        for (int j = 0; j < 32; ++j) {
-          float acc = 0.f;
-          for (int c = 0; c < C; ++c) {
-            const int d = j * C + c;
+        for (int j = 0; j < L; ++j) {
+          float acc[2] = {0.f, 0.f};
+          int have[2] = {0, 0};
+          for (int e = 0; e < 8; ++e) {
+            const int d = 8 * j + e;
             if (d >= D) break;
             const float qq = qf[h * D + d];
-            const float a = qq * lo[d];
-            const float b = qq * hi[d];
-            const float t = fmaxf(a, b);
-            acc = c == 0 ? t : acc + t;
+            const float t = fmaxf(qq * lo[d], qq * hi[d]);
+            acc[e & 1] = have[e & 1] ? acc[e & 1] + t : t;
+            have[e & 1] = 1;
           }
-          part[j] = acc;
+          part[j] = have[1] ? acc[0] + acc[1] : acc[0];
         }
-        s[h] = xor_tree32(part);
+        s[h] = xor_tree(part, L);
       }
     }
     /* lane j adds heads j, j+32, ... left to right; lanes meet in the xor tree */
