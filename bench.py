@@ -35,6 +35,7 @@ sys.path.insert(0, str(ROOT))
 METRIC = "decode tok/s at 32k ctx, 25% KV resident; miss-gather GB/s vs host-link peak"
 # configuration 2
 REQUESTS, LAYERS, CONTEXT = 16, 32, 32768
+REQUESTS_DEFAULT = REQUESTS
 Q_HEADS, KV_HEADS, HEAD_DIM, PAGE = 32, 8, 128, 16
 TOP_PAGES = 2048 // PAGE          # Quest budget of 2048 tokens incl. sink and tail
 HOT_ROWS = 2 * 2048               # reference default: 2 x max_union_rows
@@ -788,7 +789,9 @@ def run_config3(args, rank, world, local_rank, log):
     from hisparse_b200 import CacheConfig, DecodeBatch, HotConfig, RowCache, _lib
     from hisparse_b200.sharding import bind_to_device_node
 
-    c = C3
+    c = dict(C3)
+    if args.requests != REQUESTS_DEFAULT:  # fewer queries: for ncu captures only
+        c["requests"] = args.requests
     device = torch.device("cuda", local_rank)
     torch.cuda.set_device(device)
     bind_to_device_node(local_rank)
@@ -969,6 +972,8 @@ def run_config3(args, rank, world, local_rank, log):
         "config": {"workload": "config 3: isolated decode attention (resolve, miss gather, "
                                "two-phase row attention, merge) over a 64-step LRU trace, "
                                "resident fraction and page size swept",
+                   **({"reduced_for_profiling": True} if c["requests"] != C3["requests"]
+                      else {}),
                    **{k: v for k, v in c.items()}},
         "headline_point": {"page_size": 64, "resident_fraction": 0.9},
         "hbm_peak": {"gbs": hbm_peak, "source": hbm_source},
