@@ -286,13 +286,17 @@ def bytes_per_unit(valid_rows, misses):
     return meta + valid_rows * row + misses * row
 
 
-def hostlink_peak(device):
-    """Measured pinned host->device copy bandwidth (copy engine), GB/s."""
+def hostlink_peak(device, sync=None):
+    """Measured pinned host->device copy bandwidth (copy engine), GB/s: best of
+    5 copies of 1 GiB; `sync` (a barrier over the ranks) runs before each copy
+    so that concurrent measurements overlap."""
     nbytes = 1 << 30
     src = torch.empty(nbytes, dtype=torch.uint8, pin_memory=True)
     dst = torch.empty(nbytes, dtype=torch.uint8, device=device)
     best = float("inf")
     for _ in range(5):
+        if sync is not None:
+            sync()
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record()
         dst.copy_(src, non_blocking=True)
@@ -301,6 +305,31 @@ def hostlink_peak(device):
         best = min(best, a.elapsed_time(b))
     del src, dst
     return nbytes / best / 1e6
+
+
+def hostlink_peaks(device, rank, world):
+    """Host-link copy-engine bandwidth of this rank's GPU measured alone (the
+    ranks take turns) and with every rank copying at once; with the sum of
+    the concurrent rates over the ranks. One rank: the solo figure for all."""
+    solo = hostlink_peak(device) if world == 1 else None
+    if world == 1:
+        return {"solo_gbs": solo, "concurrent_gbs": solo, "aggregate_concurrent_gbs": solo}
+    import torch.distributed as dist
+
+    def sync():
+        torch.cuda.synchronize(device)
+        dist.barrier()
+
+    for r in range(world):
+        sync()
+        if r == rank:
+            solo = hostlink_peak(device)
+    sync()
+    concurrent = hostlink_peak(device, sync)
+    t = torch.tensor([concurrent], dtype=torch.float64, device=device)
+    dist.all_reduce(t)
+    return {"solo_gbs": solo, "concurrent_gbs": concurrent,
+            "aggregate_concurrent_gbs": float(t.item())}
 
 
 def run_gpu(args, rank, world, local_rank, log):
@@ -316,7 +345,8 @@ def run_gpu(args, rank, world, local_rank, log):
     local_cpus = bind_to_device_node(local_rank)
     HOST_STORE["numa_local_cpus"] = len(local_cpus) if local_cpus else None
     hbm_peak, hbm_source = measured_peaks()
-    link_peak = hostlink_peak(device)
+    links = hostlink_peaks(device, rank, world)
+    link_peak, link_concurrent = links["solo_gbs"], links["concurrent_gbs"]
     cache, mins, maxs = build_workload(device, 1 + rank, log)
     groups, batches = make_batches(cache, mins, maxs, args.microbatches, device)
     steps, warmup = args.steps, args.warmup
@@ -477,7 +507,8 @@ def run_gpu(args, rank, world, local_rank, log):
     meta_bytes = steps * LAYERS * REQUESTS * 2 * math.ceil(CONTEXT / PAGE) * KV_HEADS * \
         HEAD_DIM * 2
     quest_gbs = meta_bytes / (kernel_ms["quest"] * 1e-3) / 1e9
-    t_roof = max(hbm_bytes / (hbm_peak * 1e9), gather_bytes / (link_peak * 1e9))
+    # the step's roofline takes the host link as it is when every rank copies
+    t_roof = max(hbm_bytes / (hbm_peak * 1e9), gather_bytes / (link_concurrent * 1e9))
     step_frac = t_roof / (elapsed_ms * 1e-3)
 
     # ---- end to end: queries copied in from pinned host memory and outputs read
@@ -529,7 +560,8 @@ def run_gpu(args, rank, world, local_rank, log):
             "kernel": "gather_kernel (host->pool miss gather)", "bound": "hostlink",
             "achieved": round(live_gbs, 2),
             "peak": round(link_peak, 2), "unit": "GB/s", "frac": round(live_gbs / link_peak, 4),
-            "peak_source": "measured in bench.py: pinned host->device cudaMemcpyAsync, 1 GiB",
+            "peak_source": "measured in bench.py: pinned host->device cudaMemcpyAsync, 1 GiB, "
+                           "this GPU alone (hostlink: the same with every rank copying)",
             "traffic": round(PCIE_READ_PER_GATHERED_BYTE * live_bytes / len(live)),
             "traffic_definition": "PCIe read bytes per launch (ncu pcie__read_bytes.sum, scaled "
                                   "from a one-layer capture by the bytes gathered)",
@@ -557,8 +589,10 @@ def run_gpu(args, rank, world, local_rank, log):
                               "ms_per_launch": round(kernel_ms["quest"] / launches["quest"], 4)},
             "resolve_ms_per_launch": round(kernel_ms["resolve"] / launches["resolve"], 4),
         },
+        "hostlink": {k: round(v, 2) for k, v in links.items()},
         "step_roofline": {
-            "definition": "t_roof = max(HBM bytes / HBM peak, miss bytes / host-link peak)",
+            "definition": "t_roof = max(HBM bytes / HBM peak, miss bytes / host-link peak "
+                          "with every rank copying)",
             "hbm_bytes_per_step": int(hbm_bytes / steps),
             "hostlink_bytes_per_step": int(gather_bytes / steps), "t_roof_ms": round(
                 t_roof * 1e3 / steps, 3), "frac": round(step_frac, 4)},
@@ -601,7 +635,8 @@ def run_config5(args, rank, world, local_rank, log):
     torch.cuda.set_device(device)
     bind_to_device_node(local_rank)
     hbm_peak, _ = measured_peaks()
-    link_peak = hostlink_peak(device)
+    links = hostlink_peaks(device, rank, world)
+    link_peak = links["concurrent_gbs"]  # every rank gathers at once
     n = c["context"] // P
     hot = HotConfig(c["top_pages"] * P, c["hot_rows"])
     hot_blocks = hot.hot_blocks(P)
@@ -745,6 +780,7 @@ def run_config5(args, rank, world, local_rank, log):
                      "hbm_bytes_per_step": int(hbm_bytes),
                      "gather_gbs_avg": round(hostlink_bytes / (ms / steps * 1e-3) / 1e9, 2),
                      "hostlink_peak_gbs": round(link_peak, 2),
+                     "hostlink": {k: round(v, 2) for k, v in links.items()},
                      "t_roof_ms": round(t_roof * 1e3, 3),
                      "step_roofline_frac": round(t_roof / (ms / steps * 1e-3), 4)},
     }
@@ -1061,6 +1097,8 @@ def main():
     parser.add_argument("--warmup", type=int, default=3)
     parser.add_argument("--impl", default="hisparse_b200", choices=["hisparse_b200", "reference"])
     parser.add_argument("--no-cpu-baseline", action="store_true")
+    parser.add_argument("--no-config5", action="store_true",
+                        help="at 2 or 4 GPUs, skip the configuration-5 sub-line")
     parser.add_argument("--microbatches", type=int, default=2,
                         help="independent request groups pipelined on separate streams")
     # Smaller request/layer counts are for ncu captures only; the bench line of
@@ -1120,6 +1158,24 @@ def main():
                 print(json.dumps(result), flush=True)
             return
         result = run_gpu(args, rank, world, local_rank, log)
+        if world in (2, 4) and not args.no_config5:
+            # configuration 5 (one 1M-token request, its KV heads split over these
+            # ranks) measured after the configuration-2 line, with that workload's
+            # device and pinned host memory released first
+            import gc
+            import types
+
+            gc.collect()
+            torch.cuda.synchronize()
+            torch.cuda.empty_cache()
+            torch._C._host_emptyCache()
+            c5_args = types.SimpleNamespace(**vars(args))
+            c5_args.steps, c5_args.warmup = min(args.steps, 10), max(args.warmup, 3)
+            sub = run_config5(c5_args, rank, world, local_rank, log)
+            result["config5"] = {k: sub[k] for k in ("metric", "value", "unit", "n_gpus", "steps",
+                                                    "warmup", "ms_per_step", "scaling", "config",
+                                                    "stage_ms_per_step", "timed", "eager_tok_s",
+                                                    "per_rank")}
         os.sched_setaffinity(0, all_cpus)  # the CPU baseline uses every host core
         if rank == 0:
             if world == 1 and not args.no_cpu_baseline:

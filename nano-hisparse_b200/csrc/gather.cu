@@ -33,10 +33,11 @@ struct GatherParams {
 // Two warps of at most 64 registers (4 K registers a CTA): the gather CTAs of
 // two micro-batches fit on an SM beside a Quest or attention CTA, so the
 // kernels that overlap the gather are not held back waiting for its registers.
-// The plan is scanned 32 entries per load (one per lane, kChunks chunks per
-// warp at once): most entries are -1 padding after each request's compact
-// prefix, and a warp that read them one at a time paid an L2 round trip per
-// entry (~0.3 ms for a 64 x 4096-entry plan with nothing to move).
+// Entries are dealt to the warps round robin (entry e to warp e % warps, as a
+// request's misses form a prefix of its plan segment this spreads them over
+// every warp), and a warp reads 32 of its entries per load (lane l: entry
+// w + l * warps): reading one entry at a time cost an L2 round trip per entry
+// (~0.3 ms for a 64 x 4096-entry plan with nothing to move).
 constexpr int kChunks = 2;
 
 template <typename V>
@@ -46,13 +47,13 @@ __global__ void __launch_bounds__(kGatherThreads, 16) gather_kernel(GatherParams
   const int64_t warps = (int64_t)gridDim.x * kGatherWarps;
   const int vecs = (int)(p.row_bytes / (int64_t)sizeof(V));  // per plane
   const int64_t plane_stride = (int64_t)p.page_size * p.row_bytes;
-  const int64_t chunks = ceil_div(p.count, (int64_t)32);
-  for (int64_t c0 = warp * kChunks; c0 < chunks; c0 += warps * kChunks) {
+  const int64_t stride = 32 * kChunks * warps;  // entries one pass of this warp covers
+  for (int64_t base = warp; base < p.count; base += stride) {
     int64_t hs_[kChunks], ds_[kChunks];
 #pragma unroll
     for (int k = 0; k < kChunks; ++k) {
-      const int64_t e = (c0 + k) * 32 + lane;
-      const bool in = c0 + k < chunks && e < p.count;
+      const int64_t e = base + (int64_t)(k * 32 + lane) * warps;
+      const bool in = e < p.count;
       hs_[k] = in ? __ldcg(p.miss_host + e) : -1;
       ds_[k] = in ? __ldcg(p.miss_device + e) : -1;
     }
@@ -119,7 +120,7 @@ extern "C" int hs_gather_rows(const void *host_alias, int64_t host_blocks, void 
                  device_status};
   const uintptr_t align = reinterpret_cast<uintptr_t>(host_alias) |
                           reinterpret_cast<uintptr_t>(pool) | (uintptr_t)row_bytes;
-  const int64_t warps_needed = ceil_div(ceil_div(count, (int64_t)32), (int64_t)kChunks);
+  const int64_t warps_needed = count;
   int64_t blocks = ceil_div(warps_needed, kGatherWarps);
   // One small CTA per SM at most: enough host-link reads in flight while leaving
   // each SM room for the kernels that overlap the gather.

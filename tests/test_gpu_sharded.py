@@ -169,7 +169,7 @@ def _rank(rank, world, port, q, mn, mx, length, p, top, out):
     try:
         ks, qs = hs_slice(mn.shape[1], q.shape[0], rank, world)
         sel = sqs(q[qs].to(dev), mn[:, ks].contiguous().to(dev), mx[:, ks].contiguous().to(dev),
-                  length, p, top)
+                  length, p, top, group=dist.group.WORLD)
         out[rank] = sel.device_tokens.cpu().tolist()
     finally:
         dist.destroy_process_group()
