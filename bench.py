@@ -787,6 +787,186 @@ def run_config5(args, rank, world, local_rank, log):
 
 
 # ---------------------------------------------------------------------------
+# configuration 4: 256 requests of lognormal lengths sharded over the ranks
+# ---------------------------------------------------------------------------
+C4 = {"requests": 256, "median_context": 16384, "min_context": 4096, "max_context": 131072,
+      "sigma": 0.8, "decode_steps": 512, "seed": 4}
+
+
+def config4_lengths():
+    """The 256 requests' context lengths: lognormal (median 16k, sigma 0.8),
+    clipped to [4k, 128k], seeded; the same on every rank."""
+    rng = np.random.default_rng(C4["seed"])
+    raw = rng.lognormal(math.log(C4["median_context"]), C4["sigma"], C4["requests"])
+    return np.clip(raw, C4["min_context"], C4["max_context"]).astype(np.int64)
+
+
+def config4_pool_gib(lengths):
+    """Device pool one rank needs for its requests (25 % resident + hot blocks)."""
+    hot_blocks = math.ceil(HOT_ROWS / PAGE)
+    pages = sum(int(round(math.ceil(int(n) / PAGE) * RESIDENT_FRACTION)) + hot_blocks
+                for n in lengths)
+    return pages * LAYERS * 2 * PAGE * KV_HEADS * HEAD_DIM * 2 / 2**30
+
+
+def run_config4(args, rank, world, local_rank, log):
+    """Configuration-2 model shape serving 256 requests of lognormal lengths:
+    rank r decodes requests r, r + N, ... (no collective on the hot path), each
+    with its own tables, 25 % of its pages resident; two micro-batches per rank
+    as in configuration 2. A step decodes one token of every request of every
+    rank; the timed steps are K of the configuration's 512 (the per-step work
+    does not depend on the step's index beyond the hot-buffer warm-up)."""
+    from hisparse_b200 import CacheConfig, DecodeBatch, HotConfig, RowCache, _lib
+    from hisparse_b200.batched import DecodeGraph
+    from hisparse_b200.sharding import bind_to_device_node
+    import torch.distributed as dist
+
+    lengths_all = config4_lengths()
+    mine = lengths_all[rank::world]
+    reduced = args.requests != REQUESTS_DEFAULT
+    if reduced:  # a rank's first requests only: for functional checks and captures
+        mine = mine[:args.requests]
+    ids = list(range(len(mine)))
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    bind_to_device_node(local_rank)
+    need = config4_pool_gib(mine)
+    free = torch.cuda.mem_get_info(device)[0] / 2**30
+    base = {"metric": "decode tok/s, 256 requests of lognormal lengths (median 16k)",
+            "unit": "tok/s", "n_gpus": world, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "config 4: 256 requests sharded over the ranks, lognormal "
+                                   "lengths, configuration-2 model shape",
+                       **({"reduced_for_profiling": True} if reduced else {}), **C4,
+                       "requests_per_rank": len(mine), "pool_gib_per_rank": round(need, 1)}}
+    fits = need + 12 < free
+    if world > 1:  # every rank decides the same way
+        t = torch.tensor([1.0 if fits else 0.0], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MIN)
+        fits = bool(t.item())
+    if not fits:
+        return {**base, "value": None,
+                "unavailable": f"the pool of {len(mine)} requests per GPU needs {need:.0f} GiB "
+                               f"(25 % resident) with {free:.0f} GiB free: use 4 or more GPUs"}
+    hbm_peak, _ = measured_peaks()
+    links = hostlink_peaks(device, rank, world)
+    hot = HotConfig(TOP_PAGES * PAGE, HOT_ROWS)
+    hot_blocks = hot.hot_blocks(PAGE)
+    pages_of = [math.ceil(int(n) / PAGE) for n in mine]
+    units_pages = sum(pages_of) * LAYERS
+    page_bytes = 2 * PAGE * KV_HEADS * HEAD_DIM * 2
+    host_pages = host_store_pages(units_pages, page_bytes, log)
+    res_of = [int(round(n * RESIDENT_FRACTION)) for n in pages_of]
+    config = CacheConfig(gpu_pages=LAYERS * sum(r_ + hot_blocks for r_ in res_of),
+                         host_pages=host_pages, page_size=PAGE, kv_heads=KV_HEADS,
+                         head_dim=HEAD_DIM, device=str(device), dtype=DTYPE,
+                         index_budget_bytes=1 << 40)
+    host = torch.empty((host_pages, 2, PAGE, KV_HEADS, HEAD_DIM), dtype=DTYPE, pin_memory=True)
+    cache = RowCache(config, hot, host=host)
+    gen = torch.Generator(device=device).manual_seed(40 + rank)
+    rng = np.random.default_rng(40 + rank)
+    mins = {r: [] for r in ids}
+    maxs = {r: [] for r in ids}
+    block, offset = 0, 0
+    t0 = time.time()
+    for r in ids:
+        n, k = pages_of[r], res_of[r]
+        for layer in range(LAYERS):
+            hb = offset % (host_pages - n + 1)
+            offset += n
+            kv = torch.randn((n, 2, PAGE, KV_HEADS, HEAD_DIM), generator=gen, device=device,
+                             dtype=torch.float32).to(DTYPE)
+            mins[r].append(kv[:, 0].amin(1))
+            maxs[r].append(kv[:, 0].amax(1))
+            host[hb:hb + n].copy_(kv, non_blocking=True)
+            chosen = rng.choice(n - 2, size=k - 2, replace=False)
+            pages = np.sort(np.concatenate([chosen, [n - 2, n - 1]]))
+            resident = np.full(n, -1, dtype=np.int64)
+            resident[pages] = np.arange(block, block + k)
+            cache.pool[block:block + k] = kv.index_select(0, torch.from_numpy(pages).to(device))
+            block += k
+            hot_list = list(range(block, block + hot_blocks))
+            block += hot_blocks
+            cache.add_layer(r, layer, int(mine[r]), np.arange(hb, hb + n), resident, hot_list)
+        mins[r] = torch.stack(mins[r])
+        maxs[r] = torch.stack(maxs[r])
+        torch.cuda.synchronize(device)
+    log(f"config4: {len(mine)} requests per rank built in {time.time() - t0:.1f}s")
+    groups = [ids[i::2] for i in range(2)]
+    shared = torch.cuda.Stream(device=device)
+    batches = []
+    for g in groups:
+        streams = (torch.cuda.Stream(device=device), shared)
+        with torch.cuda.stream(streams[0]):
+            batches.append(DecodeBatch(cache, g, LAYERS, {r: mins[r] for r in g},
+                                       {r: maxs[r] for r in g}, TOP_PAGES, Q_HEADS,
+                                       streams=streams))
+    torch.cuda.synchronize(device)
+    graph = DecodeGraph(batches, LAYERS)
+    steps, warmup = args.steps, args.warmup
+    total = SETTLE_STEPS + warmup + steps
+    qgen = torch.Generator(device=device).manual_seed(400 + rank)
+    queries = [torch.randn((total, LAYERS, len(g), Q_HEADS, HEAD_DIM), generator=qgen,
+                           device=device, dtype=torch.float32).to(DTYPE) for g in groups]
+    counts = torch.zeros((total, LAYERS, len(ids), 3), dtype=torch.int64, device=device)
+
+    def run(first, last):
+        for s_ in range(first, last):
+            for i in range(len(groups)):
+                graph.queries[i].copy_(queries[i][s_])
+            graph.replay()
+            for i, g in enumerate(groups):
+                counts[s_, :, g] = graph.counts[i]
+
+    def barrier():
+        torch.cuda.synchronize(device)
+        if world > 1:
+            dist.barrier()
+
+    run(0, SETTLE_STEPS + warmup)
+    barrier()
+    sampler = ClockSampler(local_rank)
+    sampler.start()
+    sampler.wait_ready()
+    a, b_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    wall0 = time.time()
+    a.record(cache.compute)
+    run(SETTLE_STEPS + warmup, total)
+    b_.record(cache.compute)
+    barrier()
+    sampler.window(wall0, time.time())
+    clocks = sampler.stop()
+    ms = a.elapsed_time(b_)
+    if world > 1:
+        t = torch.tensor([ms], dtype=torch.float64, device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    flags = _lib.device_flags(device)
+    if flags:
+        raise RuntimeError(f"device flags raised: {flags}")
+    timed = counts[SETTLE_STEPS + warmup:].cpu().numpy()
+    row_bytes = 2 * KV_HEADS * HEAD_DIM * 2
+    misses = int(timed[..., 2].sum())
+    meta = sum(2 * n * KV_HEADS * HEAD_DIM * 2 for n in pages_of) * LAYERS * steps
+    hbm = meta + (int(timed.sum()) + misses) * row_bytes
+    hostb = misses * row_bytes
+    t_roof = max(hbm / (hbm_peak * 1e9), hostb / (links["concurrent_gbs"] * 1e9))
+    sums = torch.tensor([len(ids) * steps, misses, hbm, hostb], dtype=torch.float64,
+                        device=device)
+    if world > 1:
+        dist.all_reduce(sums)
+    tokens = float(sums[0].item())
+    return {**base, "value": round(tokens / (ms * 1e-3), 2), "steps": steps, "warmup": warmup,
+            "ms_per_step": round(ms / steps, 3), "clocks": clocks,
+            "hostlink": {k_: round(v, 2) for k_, v in links.items()},
+            "per_rank": {"requests": len(ids), "context_tokens": int(sum(int(n) for n in mine)),
+                         "miss_rows_per_unit": round(misses / (steps * LAYERS * len(ids)), 1),
+                         "hbm_bytes_per_step": int(hbm / steps),
+                         "hostlink_bytes_per_step": int(hostb / steps),
+                         "step_roofline_frac": round(t_roof / (ms * 1e-3), 4)}}
+
+
+# ---------------------------------------------------------------------------
 # configuration 3: isolated decode attention, resident-fraction sweep
 # ---------------------------------------------------------------------------
 C3 = {"requests": 64, "q_heads": 32, "kv_heads": 8, "head_dim": 128, "context": 131072,
@@ -1106,11 +1286,12 @@ def main():
     parser.add_argument("--transfer", choices=["shared", "separate"], default=TRANSFER,
                         help="one transfer stream for all micro-batches (gathers take the "
                              "host link in turn) or one each")
-    parser.add_argument("--workload", choices=["config2", "config3", "config5"],
+    parser.add_argument("--workload", choices=["config2", "config3", "config4", "config5"],
                         default="config2",
                         help="config2 (the bench line), config3 (isolated decode attention, "
-                             "resident-fraction sweep) or config5 (one 1M-token request, KV "
-                             "heads split over 1, 2 or 4 GPUs)")
+                             "resident-fraction sweep), config4 (256 requests sharded over the "
+                             "GPUs) or config5 (one 1M-token request, KV heads split over 1, 2 "
+                             "or 4 GPUs)")
     parser.add_argument("--requests", type=int, default=REQUESTS)
     parser.add_argument("--layers", type=int, default=LAYERS)
     args = parser.parse_args()
@@ -1151,8 +1332,9 @@ def main():
                                 device_id=torch.device("cuda", local_rank))
     try:
         all_cpus = os.sched_getaffinity(0)
-        if args.workload in ("config3", "config5"):
-            run = run_config3 if args.workload == "config3" else run_config5
+        if args.workload in ("config3", "config4", "config5"):
+            run = {"config3": run_config3, "config4": run_config4,
+                   "config5": run_config5}[args.workload]
             result = run(args, rank, world, local_rank, log)
             if rank == 0:
                 print(json.dumps(result), flush=True)

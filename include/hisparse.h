@@ -142,7 +142,8 @@ HS_API int hs_quest_select(const void *query, int query_dtype, const void *minim
 /* Batched over `batch` requests of one layer. query is [batch, q_heads,
  * head_dim] with `query_batch_stride` elements between requests;
  * minimum_ptrs/maximum_ptrs are device arrays of `batch` pointers to each
- * request's [>= max_pages, kv_heads, head_dim] metadata, each 16-byte aligned
+ * request's [pages, kv_heads, head_dim] metadata (pages >= ceil(length / page_size) of
+ * that request; max_pages >= every request's pages), each 16-byte aligned
  * (bulk copies read them; a misaligned request raises HS_DEV_MISALIGNED and
  * is skipped); lengths is a device int32[batch]. out_tokens is
  * [batch, out_capacity], out_counts int32[batch]. */
@@ -219,8 +220,9 @@ HS_API int hs_resolve_rows(const void *positions, int positions_dtype, int64_t c
 
 /* Batched: positions int32 [batch, count]; per-request tables as device
  * pointer arrays; lengths device int32[batch]; outputs [batch, count] and
- * out_counts [batch, 3]. table_pages is a capacity every request's
- * source/resident tables satisfy. out_ready (optional, [batch, count]) receives
+ * out_counts [batch, 3]. Each request's source/resident tables cover its own
+ * ceil(length / page_size) pages; table_pages bounds every request's pages.
+ * out_ready (optional, [batch, count]) receives
  * the physical rows that need no gather (resident and hot hits), compact in
  * sorted logical order and -1 padded: out_counts[b][0] + out_counts[b][1] of
  * them; with miss_device (out_counts[b][2] rows) it lets attention over the

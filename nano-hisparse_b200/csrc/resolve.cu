@@ -253,12 +253,15 @@ __device__ __forceinline__ void resolve_body(const ResolveParams &p, const Layou
   // ---- 3. per sorted entry: dedupe and page lookups; hash of the hot tags ------
   for (int j = tid; j < K; j += nthreads) {
     const int64_t v = keys[j];
-    const bool unique = v < length && (j == 0 || keys[j - 1] != keys[j]);
-    int64_t page = v / P;
+    const bool causal = v < length;  // keys are normalised to [0, length] or INT32_MAX
+    const bool unique = causal && (j == 0 || keys[j - 1] != keys[j]);
+    // only causal keys read the tables: a request's tables cover its own pages
+    // (ceil(length / P)), which may be fewer than table_pages
+    int64_t page = causal ? v / P : 0;
     if (page > p.table_pages - 1) page = p.table_pages - 1;
     const int64_t offset = v % P;
-    const int64_t source = src_tab[page];
-    const int64_t resident = res_tab[page];
+    const int64_t source = causal ? (int64_t)src_tab[page] : -1;
+    const int64_t resident = causal ? (int64_t)res_tab[page] : -1;
     uint8_t f = 0;
     int64_t phys = -1;
     if (unique && source >= 0) {

@@ -40,7 +40,18 @@ class _LayerState:
         self.hot_ptrs = _pointers([t.hot for t in tables], device)
         self.tag_ptrs = _pointers([t.tags for t in tables], device)
         self.lru_ptrs = _pointers([t.lru for t in tables], device)
-        self.table_pages = min(int(t.source.numel()) for t in tables)
+        # Requests may have tables of different sizes (each covers its own pages):
+        # the kernels read a request's tables only below ceil(length / P), so the
+        # batch passes the largest capacity and every request is checked here.
+        page = cache.config.page_size
+        for r, t in zip(ids, tables):
+            pages = -(-cache.lengths[r, layer] // page)
+            own = min(int(t.source.numel()), int(t.resident.numel()),
+                      int(batch.minimum[r][layer].shape[0]), int(batch.maximum[r][layer].shape[0]))
+            if pages > own:
+                raise ValueError(f"request {r!r} layer {layer}: {pages} pages of history exceed "
+                                 f"its tables ({own} pages)")
+        self.table_pages = max(int(t.source.numel()) for t in tables)
         self.lengths = torch.tensor([cache.lengths[r, layer] for r in ids], dtype=torch.int32,
                                     device=device)
         self.counts = torch.zeros((len(ids), 3), dtype=torch.int64, device=device)
@@ -81,7 +92,7 @@ class DecodeBatch:
         self.width = top_pages * cfg.page_size
         if self.width > cache.hot_config.max_union_rows:
             raise ValueError("top-k width/union exceeds the admitted max_union_rows")
-        self.max_pages = min(int(minimum[r].shape[1]) for r in self.request_ids)
+        self.max_pages = max(int(minimum[r].shape[1]) for r in self.request_ids)
         self.hot_rows = cache.hot_config.hot_rows
         self.layers = [_LayerState(self, layer) for layer in range(layers)]
         lib = _lib.load()
@@ -118,7 +129,10 @@ class DecodeBatch:
         self._row_bytes = cfg.row_bytes
 
     def set_lengths(self, layer: int, lengths: torch.Tensor):
-        """Device int32 [B] context lengths of `layer` (after an append)."""
+        """Device int32 [B] context lengths of `layer` (after an append). Each
+        request's pages of history must stay within its own tables (checked on
+        the host when the batch is built; a device-side length past them is
+        flagged HS_DEV_PAGES_EXCEED_TABLE only against the batch's largest)."""
         self.layers[layer].lengths.copy_(lengths)
 
     def layer(self, layer: int, query: torch.Tensor, out: torch.Tensor | None = None,
