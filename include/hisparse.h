@@ -306,7 +306,9 @@ HS_API int hs_attend_merge(int batch, int phases, void *out, int64_t out_batch_s
  *   kv_batch_stride elements after b-1; a row is kv_heads*head_dim elements);
  *   when host_block[b] >= 0 the same rows of host block host_block[b] (through
  *   host_alias, the hs_host_device_pointer alias) take the same values — the
- *   host mirror, written by the kernel itself;
+ *   host mirror, written by the kernel itself. pool_block[b] < 0 makes the
+ *   chunk host-only (a page that holds no pool block): it then needs a
+ *   host block, and its earlier rows for the summary are read there;
  *   minimum_ptrs[b] / maximum_ptrs[b] point to the page's [kv_heads, head_dim]
  *   bounds in the KV dtype: min/max of the new K rows folded in exactly as
  *   torch.minimum(old, new) / torch.maximum(old, new) (NaN propagates, an equal

@@ -42,29 +42,33 @@ __global__ void __launch_bounds__(kAppendThreads) append_kernel(AppendParams p) 
   const int cnt = p.count[b], w = p.within[b];
   if (cnt <= 0) return;
   const int64_t blk = p.pool_block[b], hb = p.host_block[b];
-  if (w < 0 || w + cnt > p.page_size || blk < 0 || blk >= p.pool_blocks ||
-      (hb >= 0 && (p.host == nullptr || hb >= p.host_blocks))) {
+  // pool_block < 0: a host-only chunk (a page with no pool block), which needs a host block
+  const bool host_ok = hb >= 0 && p.host != nullptr && hb < p.host_blocks;
+  if (w < 0 || w + cnt > p.page_size || blk >= p.pool_blocks || (hb >= 0 && !host_ok) ||
+      (blk < 0 && !host_ok)) {
     if (e == 0) flag(p.status, HS_DEV_ROW_OUT_OF_RANGE);
     return;
   }
   const int64_t E = p.elems, plane = (int64_t)p.page_size * E;
-  T *pk = reinterpret_cast<T *>(p.pool) + blk * 2 * plane;
-  T *pv = pk + plane;
+  T *pk = blk >= 0 ? reinterpret_cast<T *>(p.pool) + blk * 2 * plane : nullptr;
   T *hk = hb >= 0 ? reinterpret_cast<T *>(p.host) + hb * 2 * plane : nullptr;
+  const T *page_k = pk != nullptr ? pk : hk;  // where the page's earlier rows live
   const T *k = static_cast<const T *>(p.k) + (int64_t)b * p.kv_batch_stride;
   const T *v = static_cast<const T *>(p.v) + (int64_t)b * p.kv_batch_stride;
 
   // rows 0 .. w-1 already in the page come first in the mean
   float sum = 0.f;
-  for (int r = 0; r < w; ++r) sum += to_f32(pk[(int64_t)r * E + e]);
+  for (int r = 0; r < w; ++r) sum += to_f32(page_k[(int64_t)r * E + e]);
   T lo = k[e], hi = k[e];
   bool nan_seen = false;
   T nan_value = lo;
   for (int i = 0; i < cnt; ++i) {
     const T kx = k[(int64_t)i * E + e], vx = v[(int64_t)i * E + e];
     const int64_t row = (int64_t)(w + i) * E + e;
-    pk[row] = kx;
-    pv[row] = vx;
+    if (pk != nullptr) {
+      pk[row] = kx;
+      pk[plane + row] = vx;
+    }
     if (hk != nullptr) {
       hk[row] = kx;
       hk[plane + row] = vx;

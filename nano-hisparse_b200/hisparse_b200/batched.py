@@ -135,6 +135,17 @@ class DecodeBatch:
         flagged HS_DEV_PAGES_EXCEED_TABLE only against the batch's largest)."""
         self.layers[layer].lengths.copy_(lengths)
 
+    def bind_lengths(self, lengths: torch.Tensor):
+        """Makes every layer read its context lengths from `lengths` (device
+        int32 [B]): in decode all layers of a request have the same length, so
+        a decode loop updates one tensor per step instead of one per layer."""
+        if (lengths.dtype != torch.int32 or tuple(lengths.shape) != (self.batch,)
+                or lengths.device != self.device or not lengths.is_contiguous()):
+            raise ValueError("lengths must be a contiguous int32 [batch] tensor on the "
+                             "batch's device")
+        for st in self.layers:
+            st.lengths = lengths
+
     def layer(self, layer: int, query: torch.Tensor, out: torch.Tensor | None = None,
               counts: torch.Tensor | None = None, timing: list | None = None,
               stages=None, serial: bool = False, part: str = "all",

@@ -252,24 +252,26 @@ def append_rows(k, v, within, block, host_block, minimum, maximum, summary):
     """One page chunk of HostStore.append (storage.py:296-321), on copies.
 
     k, v: [count, Hkv, D] torch rows; block / host_block: the page's pool block
-    and host block [2, P, Hkv, D] (host_block may be None); minimum / maximum:
+    and host block [2, P, Hkv, D] (host_block may be None; block None makes
+    the chunk host-only, which needs a host_block); minimum / maximum:
     [Hkv, D] in the KV dtype; summary: [Hkv, D] float32 (numpy arrays
     and torch tensors; 16-bit data comes back as uint16 bit patterns) — see
     as_array. Returns (block, host_block, minimum, maximum, summary)."""
     import torch
 
     dtype = {torch.float32: F32, torch.float16: F16, torch.bfloat16: BF16}[k.dtype]
-    arrays = [as_array(t)[0] for t in (k, v, block, minimum, maximum)]
-    host = None if host_block is None else as_array(host_block)[0]
+    arrays = [as_array(t)[0] for t in (k, v, minimum, maximum)]
+    blk = None if block is None else np.ascontiguousarray(as_array(block)[0]).copy()
+    host = None if host_block is None else np.ascontiguousarray(as_array(host_block)[0]).copy()
     summ = np.ascontiguousarray(summary.numpy() if hasattr(summary, "numpy") else summary,
                                 dtype=np.float32).copy()
-    kk, vv, blk, mn, mx = [np.ascontiguousarray(a).copy() for a in arrays]
-    if host is not None:
-        host = np.ascontiguousarray(host).copy()
+    kk, vv, mn, mx = [np.ascontiguousarray(a).copy() for a in arrays]
     elems = kk[0].size if kk.shape[0] else int(np.prod(kk.shape[1:]))
-    rc = lib().or_append_rows(_ptr(kk), _ptr(vv), dtype, kk.shape[0], within, _ptr(blk),
+    page = blk if blk is not None else host
+    rc = lib().or_append_rows(_ptr(kk), _ptr(vv), dtype, kk.shape[0], within,
+                              None if blk is None else _ptr(blk),
                               None if host is None else _ptr(host), _ptr(mn), _ptr(mx),
-                              _ptr(summ), elems, blk.shape[1])
+                              _ptr(summ), elems, page.shape[1])
     if rc:
         raise ValueError(f"or_append_rows failed ({rc})")
     return blk, host, mn, mx, summ

@@ -450,7 +450,8 @@ int or_gather_rows(const uint8_t *host, int64_t host_blocks, uint8_t *pool, int6
  * One page chunk of HostStore.append (storage.py:296-321): rows
  * within .. within+count-1 of the K and V planes of `block` (one pool block,
  * [2, P, E] elements, E = kv_heads*head_dim) take the count rows of k and v
- * ([count, E]); `host_block` (NULL: no mirror) receives the same rows; then
+ * ([count, E]); `host_block` (NULL: no mirror) receives the same rows; with
+ * `block` NULL the chunk is host-only and `host_block` holds the page; then
  *   minimum[e] = min(minimum[e], min_i k[i][e]) and maximum likewise — exact
  *   in the KV dtype, NaN propagating, an equal new value replacing the old
  *   (torch.minimum / torch.maximum of old and new);
@@ -465,12 +466,16 @@ int or_append_rows(const void *k, const void *v, int dtype, int64_t count, int64
                    void *block, void *host_block, void *minimum, void *maximum,
                    float *summary, int64_t elems, int P) {
   if (count < 0 || within < 0 || within + count > P || elems < 1) return 1;
+  if (!block && !host_block) return 1;
   const int64_t es = dtype == OR_F32 ? 4 : 2;
-  uint8_t *blk = (uint8_t *)block;
+  uint8_t *blk = (uint8_t *)(block ? block : host_block); /* the page's rows for the mean */
   const int64_t plane = (int64_t)P * elems * es, row = elems * es;
   for (int64_t i = 0; i < count; ++i) {
-    memcpy(blk + (within + i) * row, (const uint8_t *)k + i * row, (size_t)row);
-    memcpy(blk + plane + (within + i) * row, (const uint8_t *)v + i * row, (size_t)row);
+    if (block) {
+      memcpy((uint8_t *)block + (within + i) * row, (const uint8_t *)k + i * row, (size_t)row);
+      memcpy((uint8_t *)block + plane + (within + i) * row, (const uint8_t *)v + i * row,
+             (size_t)row);
+    }
     if (host_block) {
       memcpy((uint8_t *)host_block + (within + i) * row, (const uint8_t *)k + i * row, (size_t)row);
       memcpy((uint8_t *)host_block + plane + (within + i) * row, (const uint8_t *)v + i * row,

@@ -24,6 +24,15 @@ weights_only=True):
                       test_trace.py), with the final row counters
   append_cases.pt     every HostStore.append (storage.py:296-321) of scripted
                       prefill + decode sessions, with the state before/after
+  engine_cases.pt     Engine.run (engine.py:76-136) at configuration 1 (the
+                      reference's CPU demo: 3 requests of 96/128/160 tokens,
+                      33 tokens each, Quest top_k 4) and variants (a pool
+                      holding all three, an EOS token, full history): every
+                      step's emitted (request, token) list with the
+                      reference's top-2 logit margin, on weights made by
+                      hisparse_b200.engine.DecoderWeights.random (seeded,
+                      exact in fp32, rebuilt by the tests without the
+                      reference) loaded into the reference Model
   quest_full_cases.pt quest_selection at the full sizes the bench runs
                       (configuration 2: 2,048-2,050 pages; configuration 3:
                       8,192 / 2,048 pages; configuration 5: 16,389 pages), on
@@ -241,6 +250,101 @@ def quest_full_cases(ref):
                 case[f"pages_{int(sink)}"] = sel.pages
             cases.append(case)
             print(f"  {case['name']}: {pages} pages", flush=True)
+    return cases
+
+
+# ---------------------------------------------------------------------------
+# engine
+# ---------------------------------------------------------------------------
+ENGINE_MODEL = dict(vocab_size=1024, hidden_size=256, intermediate_size=512,
+                    num_hidden_layers=4, num_attention_heads=8, num_key_value_heads=2)
+# name, gpu_pages, top_k, prompt lengths, max_new_tokens, eos (None, or the
+# generated token of (case, request, index) to stop on)
+ENGINE_RUNS = [
+    ("config1", 24, 4, (96, 128, 160), 33, None),
+    ("config1_wide", 120, 4, (96, 128, 160), 33, None),
+    ("config1_eos", 120, 4, (96, 128, 160), 33, ("config1_wide", "b", 5)),
+    ("full_history", 64, None, (20, 9, 31), 12, None),
+]
+
+
+def engine_cases(ref, seed=1):
+    """seed 1 (weights and prompts) of seeds 0-5 leaves the widest margins for
+    a device run to land on the same tokens: smallest top-2 logit gap 2.8e-3,
+    smallest Quest boundary gap 7.8e-5 of the largest page score (seed 0:
+    2.5e-4 and 1.3e-5), against fp32 device-vs-CPU differences near 1e-6."""
+    from nano_hisparse import model as model_mod
+    from nano_hisparse.config import CacheConfig
+    from nano_hisparse.engine import Engine
+    from nano_hisparse.hybrid import HotConfig, HybridKVCache
+
+    sys.path.insert(0, str(OUT.parent))
+    sys.path.insert(0, str(OUT.parent.parent / "nano-hisparse_b200"))
+    from helpers import forced_pages, quest_scores_fp64, weights_digest
+    from hisparse_b200.engine import DecoderConfig, DecoderWeights
+
+    weights = DecoderWeights.random(DecoderConfig(**ENGINE_MODEL), seed, device="cpu",
+                                    dtype=torch.float32)
+    model = model_mod.Model(model_mod.ModelConfig(**ENGINE_MODEL)).eval()
+    model.load_state_dict(weights.state_dict())
+    original_quest, original_emit = model_mod.quest_selection, Engine._emit
+    gaps, margins = [], []
+
+    def quest(query, minimum, maximum, length, page_size, top_pages, keep_sink=True):
+        sel = original_quest(query, minimum, maximum, length, page_size, top_pages, keep_sink)
+        pages = math.ceil(length / page_size)
+        scores = quest_scores_fp64(query, minimum, maximum, pages)
+        forced = forced_pages(pages, top_pages, keep_sink)
+        chosen = [p for p in sel.pages if p not in forced]
+        others = [p for p in range(pages) if p not in forced and p not in sel.pages]
+        if chosen and others:
+            scale = max(float(np.abs(scores).max()), 1e-30)
+            gaps.append(float((min(scores[chosen]) - max(scores[others])) / scale))
+        return sel
+
+    def emit(self, request, logits):
+        top = logits.topk(2).values
+        margins.append(float(top[0] - top[1]))
+        return original_emit(self, request, logits)
+
+    cases, done = [], {}
+    model_mod.quest_selection, Engine._emit = quest, emit
+    try:
+        for name, gpu_pages, top_k, lengths, max_new, eos in ENGINE_RUNS:
+            gen = torch.Generator().manual_seed(seed)
+            prompts = [torch.randint(0, ENGINE_MODEL["vocab_size"], (n,), generator=gen).tolist()
+                       for n in lengths]
+            eos_token = None if eos is None else done[eos[0]]["generated"][eos[1]][eos[2]]
+            cache = HybridKVCache(CacheConfig(gpu_pages=gpu_pages, host_pages=256,
+                                              page_size=16, kv_heads=2, head_dim=32,
+                                              device="cpu", dtype=torch.float32),
+                                  HotConfig(64, 64))
+            engine = Engine(model, cache, top_k=top_k, eos_token_id=eos_token)
+            ids = ["a", "b", "c"]
+            for rid, prompt in zip(ids, prompts):
+                engine.add_request(rid, prompt, max_new)
+            gaps.clear()
+            steps = []
+            while engine.waiting or engine.running:
+                margins.clear()
+                emitted = engine.step()
+                steps.append([(rid, tok, m) for (rid, tok), m in zip(emitted, margins)])
+            cache.collect(wait=True)
+            case = {"name": name, "model": dict(ENGINE_MODEL), "seed": seed,
+                    "weights_sha256": weights_digest(weights),
+                    "gpu_pages": gpu_pages, "host_pages": 256, "page_size": 16,
+                    "union": 64, "hot_rows": 64, "top_k": top_k, "eos_token_id": eos_token,
+                    "requests": [(rid, p, max_new) for rid, p in zip(ids, prompts)],
+                    "steps": steps,
+                    "generated": {r: engine.requests[r].generated for r in ids},
+                    "min_logit_margin": min(m for step in steps for *_, m in step),
+                    "min_quest_gap": min(gaps) if gaps else None}
+            done[name] = case
+            cases.append(case)
+            print(f"  {name}: {len(steps)} steps, min margin {case['min_logit_margin']:.3e}, "
+                  f"min Quest gap {case['min_quest_gap']}", flush=True)
+    finally:
+        model_mod.quest_selection, Engine._emit = original_quest, original_emit
     return cases
 
 
@@ -611,7 +715,8 @@ def main():
     torch.set_num_threads(4)
     for name, fn in [("resolver_cases", resolver_cases), ("quest_cases", quest_cases),
                      ("attention_cases", attention_cases), ("scenarios", scenarios),
-                     ("append_cases", append_cases), ("quest_full_cases", quest_full_cases)]:
+                     ("append_cases", append_cases), ("quest_full_cases", quest_full_cases),
+                     ("engine_cases", engine_cases)]:
         if args.only and name not in args.only:
             continue
         data = fn(ref)

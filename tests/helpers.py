@@ -121,3 +121,15 @@ def near_tie_report(expected_tokens, got_tokens, query, minimum, maximum, length
                      f"{(scores[p] - kth) / max(abs(kth), 1e-30):+.3e} (relative)"
                      + (" [forced]" if p in forced else "")
                      for p in sorted(a ^ b))
+
+
+def weights_digest(weights) -> str:
+    """sha256 of a DecoderWeights' reference state_dict (fp32 bytes, sorted
+    names): pins that seeded weights come out the same on every machine."""
+    import hashlib
+
+    h = hashlib.sha256()
+    for name, tensor in sorted(weights.state_dict().items()):
+        h.update(name.encode())
+        h.update(tensor.numpy().tobytes())
+    return h.hexdigest()

@@ -128,6 +128,63 @@ def test_decode_append_batch_matches_oracle(dtype):
     assert not _lib.device_flags(DEV)
 
 
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_host_only_chunks_match_oracle(dtype):
+    """Chunks of pages that hold no pool block (pool_block -1): the rows go to
+    the host block only and the mean reads the page's earlier rows there;
+    pooled chunks of the same launch are unaffected, and a chunk with neither
+    block is skipped and flagged."""
+    gen = torch.Generator().manual_seed(23)
+    b, p, hkv, d, blocks = 12, 16, 2, 64, 32
+    config = CacheConfig(gpu_pages=blocks, host_pages=blocks, page_size=p, kv_heads=hkv,
+                         head_dim=d, device=DEV, dtype=dtype)
+    pool_cpu = torch.randn(blocks, 2, p, hkv, d, generator=gen).to(dtype)
+    host_cpu = torch.randn(blocks, 2, p, hkv, d, generator=gen).to(dtype)
+    slots = torch.randperm(blocks, generator=gen)[:b]
+    slots[::2] = -1
+    host_slots = torch.randperm(blocks, generator=gen)[:b]
+    within = torch.randint(0, p - 3, (b,), generator=gen)
+    count = torch.randint(1, 4, (b,), generator=gen)
+    k = torch.randn(b, 3, hkv, d, generator=gen).to(dtype)
+    v = torch.randn(b, 3, hkv, d, generator=gen).to(dtype)
+    mn_cpu = torch.full((b, hkv, d), float("inf")).to(dtype)
+    mx_cpu = torch.full((b, hkv, d), float("-inf")).to(dtype)
+    sm_cpu = torch.zeros(b, hkv, d)
+    pool, host = pool_cpu.to(DEV), host_cpu.pin_memory()
+    mn, mx, sm = mn_cpu.to(DEV), mx_cpu.to(DEV), sm_cpu.to(DEV)
+    ptrs = [torch.tensor([t[i].data_ptr() for i in range(b)], dtype=torch.int64, device=DEV)
+            for t in (mn, mx, sm)]
+    append_chunks(k.to(DEV), v.to(DEV), within.to(torch.int32).to(DEV),
+                  count.to(torch.int32).to(DEV), slots.to(DEV), pool, *ptrs, config,
+                  MappedHost(host), host_slots.to(DEV))
+    torch.cuda.synchronize()
+    for i in range(b):
+        s, h, w, c = int(slots[i]), int(host_slots[i]), int(within[i]), int(count[i])
+        blk, hst, omn, omx, osm = oracle.append_rows(
+            k[i, :c], v[i, :c], w, None if s < 0 else pool_cpu[s], host_cpu[h], mn_cpu[i],
+            mx_cpu[i], sm_cpu[i].numpy())
+        if s >= 0:
+            assert np.array_equal(oracle.as_array(pool[s].cpu())[0], blk)
+        assert np.array_equal(oracle.as_array(host[h])[0], hst)
+        assert np.array_equal(oracle.as_array(mn[i].cpu())[0], omn)
+        assert np.array_equal(oracle.as_array(mx[i].cpu())[0], omx)
+        assert np.array_equal(sm[i].cpu().numpy(), osm)
+    untouched = set(range(blocks)) - {int(x) for x in slots if x >= 0}
+    for s in untouched:
+        assert torch.equal(pool[s].cpu(), pool_cpu[s])
+    assert not _lib.device_flags(DEV)
+    # neither a pool nor a host block: skipped, flagged, nothing written
+    before = mn.clone()
+    append_chunks(k[:1].to(DEV), v[:1].to(DEV), torch.zeros(1, dtype=torch.int32, device=DEV),
+                  torch.ones(1, dtype=torch.int32, device=DEV),
+                  torch.tensor([-1], dtype=torch.int64, device=DEV), pool,
+                  *[t[:1] for t in ptrs], config, MappedHost(host),
+                  torch.tensor([-1], dtype=torch.int64, device=DEV))
+    torch.cuda.synchronize()
+    assert _lib.device_flags(DEV) == [_lib.DEVICE_FLAGS[1]]
+    assert torch.equal(mn, before)
+
+
 def test_append_rejects_chunks_leaving_their_page():
     config = CacheConfig(gpu_pages=2, host_pages=2, page_size=4, kv_heads=1, head_dim=8,
                          device=DEV, dtype=torch.float32)
