@@ -39,6 +39,10 @@ weights_only=True):
                       inputs regenerated from a seed by
                       tests/helpers.full_quest_inputs; each case records the
                       seed, the inputs' sha256 and the reference's pages
+  trace_reports.pt    replay_trace (trace.py:109-216) reports, without the
+                      device name and the attention-error column, on the
+                      README's synthetic traces and on seeded traces of other
+                      dtypes, page sizes and schemas, each with its trace
 """
 
 from __future__ import annotations
@@ -705,6 +709,87 @@ def append_cases(ref):
     return out
 
 
+# ---------------------------------------------------------------------------
+# trace replay reports (trace.py:109-216)
+# ---------------------------------------------------------------------------
+def trace_reports(ref):
+    """The reference's replay_trace report (locality, counters and hot
+    contents per event, and the summary) on the five README traces of
+    synthetic_trace at the README's capacities and at the default capacity,
+    and on seeded traces of other shapes: bf16 and fp16 KV with two KV heads,
+    odd page sizes, a schema-1 trace (per-head position lists) and a trace
+    that selects rows of the write tail. Each case stores the trace it
+    replayed."""
+    from nano_hisparse.trace import replay_trace, synthetic_trace
+
+    torch.set_num_threads(1)
+    out = []
+
+    def report_of(trace, capacity):
+        report = replay_trace(trace, capacity, "cpu")
+        for event in report["events"]:
+            event.pop("max_abs_error")
+            event["positions"] = [list(h) for h in event["positions"]] \
+                if event["positions"] and isinstance(event["positions"][0], tuple) \
+                else list(event["positions"])
+        report["summary"].pop("max_abs_error")
+        report.pop("device")
+        return report
+
+    for pattern, capacity in [("reuse", 4), ("alternating", 4), ("alternating", 8),
+                              ("streaming", 8), ("packed", 4), ("reuse", None),
+                              ("streaming", None)]:
+        trace = synthetic_trace(pattern)
+        out.append({"name": f"synthetic_{pattern}_{capacity}", "capacity": capacity,
+                    "trace": trace, "report": report_of(trace, capacity)})
+
+    def seeded(seed, dtype, prefill, heads, kv_heads, dim, page, steps, picks, schema=2,
+               recent=False):
+        g = torch.Generator().manual_seed(seed)
+
+        def kv(count):
+            return torch.randn(count, kv_heads, dim, generator=g).to(dtype)
+
+        trace = {"schema_version": schema, "source": {"kind": "seeded", "seed": seed},
+                 "page_size": page, "prefill": {"k": kv(prefill), "v": kv(prefill)},
+                 "events": []}
+        previous = None
+        for step in range(steps):
+            length = prefill + step + 1
+            if schema == 2:
+                if previous is not None and step % 3:
+                    keep = [t for t in previous if torch.rand((), generator=g) < 0.7]
+                else:
+                    keep = []
+                fresh = torch.randint(0, length, (picks,), generator=g).tolist()
+                if recent:
+                    fresh += [length - 1, length - 2]
+                rows = sorted(set(keep + fresh))[:picks]
+                previous = rows
+            else:
+                rows = [sorted(set(torch.randint(0, length, (picks // heads + 1,),
+                                                 generator=g).tolist()))
+                        for _ in range(heads)]
+            trace["events"].append({"q": torch.randn(heads, dim, generator=g).to(dtype),
+                                    "k": kv(1), "v": kv(1), "positions": rows})
+        return trace
+
+    for name, args, capacity in [
+        ("bf16_p3", dict(seed=11, dtype=torch.bfloat16, prefill=50, heads=4, kv_heads=2, dim=16,
+                         page=3, steps=8, picks=12), 12),
+        ("fp16_p5", dict(seed=12, dtype=torch.float16, prefill=70, heads=6, kv_heads=2, dim=24,
+                         page=5, steps=8, picks=16), 20),
+        ("f32_p4_recent", dict(seed=13, dtype=torch.float32, prefill=40, heads=2, kv_heads=1,
+                               dim=8, page=4, steps=8, picks=10, recent=True), None),
+        ("schema1_p4", dict(seed=14, dtype=torch.float32, prefill=48, heads=4, kv_heads=2,
+                            dim=8, page=4, steps=6, picks=8, schema=1), 16),
+    ]:
+        trace = seeded(**args)
+        out.append({"name": f"seeded_{name}", "capacity": capacity, "trace": trace,
+                    "report": report_of(trace, capacity)})
+    return out
+
+
 def main():
     parser = argparse.ArgumentParser(description=__doc__.split("\n\n")[0])
     parser.add_argument("--reference", required=True,
@@ -716,7 +801,7 @@ def main():
     for name, fn in [("resolver_cases", resolver_cases), ("quest_cases", quest_cases),
                      ("attention_cases", attention_cases), ("scenarios", scenarios),
                      ("append_cases", append_cases), ("quest_full_cases", quest_full_cases),
-                     ("engine_cases", engine_cases)]:
+                     ("engine_cases", engine_cases), ("trace_reports", trace_reports)]:
         if args.only and name not in args.only:
             continue
         data = fn(ref)
