@@ -12,14 +12,19 @@ miss gather and row attention on the sm_100a kernels:
                                                                      447-451; attention.py:22-25)
   nano_hisparse.storage.HostStore.append                            (hybrid.py:391)
 
-The reference's residency policy, storage, model and engine are untouched.
-``uninstall`` restores the original bindings.
+With ``indexed_residency`` (the default) it also installs
+``hisparse_b200.residency``: the same residency policy, with its per-layer
+scans over every page (hybrid.py:204-223, 276-277, 423-427) answered from a
+per-layer index of resident pages. The policy's decisions, the storage,
+model and engine are the reference's. ``uninstall`` restores the original
+bindings.
 """
 
 from __future__ import annotations
 
 import importlib
 
+from . import residency
 from . import row_kernels as _rk
 from .append import host_store_append
 from .row_index import LogicalTopK, resolve_rows
@@ -38,7 +43,7 @@ _BINDINGS = [
 _saved: dict = {}
 
 
-def install(package) -> list[str]:
+def install(package, *, indexed_residency=True) -> list[str]:
     """Rebind the reference's hot-path names; returns the names rebound.
 
     ``package`` is the imported reference package (``import nano_hisparse``).
@@ -54,6 +59,8 @@ def install(package) -> list[str]:
                                                                                        name)
         setattr(owner, name, replacement)
         done.append(f"{module_name}.{attr}")
+    if indexed_residency:
+        done += residency.install(package)
     return done
 
 
@@ -67,6 +74,7 @@ def _owner(package_name, module_name, attr):
 
 
 def uninstall(package) -> None:
+    residency.uninstall(package)
     for (pkg, module_name, attr), original in list(_saved.items()):
         if pkg != package.__name__:
             continue

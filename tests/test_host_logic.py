@@ -86,7 +86,7 @@ def test_plugin_rebinds_and_restores_reference_names():
                                                            {"append": store_append})
     sys.modules["fake_reference"] = pkg
     try:
-        bound = plugin.install(pkg)
+        bound = plugin.install(pkg, indexed_residency=False)
         assert len(bound) == 8
         import hisparse_b200 as hs
         from hisparse_b200.append import host_store_append

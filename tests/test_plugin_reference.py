@@ -126,10 +126,15 @@ def test_install_and_uninstall_on_the_reference(reference):
     originals = {(m, a): _original(reference, m, a) for m, a, _ in plugin._BINDINGS}
     bound = plugin.install(reference)
     try:
-        assert sorted(bound) == sorted(f"{m}.{a}" for m, a, _ in plugin._BINDINGS)
+        indexed = ["DeviceAllocator.bind", "DeviceAllocator.release",
+                   "HybridKVCache._historical_pages", "HybridKVCache.update_residency",
+                   "HybridKVCache.resolve"]
+        assert sorted(bound) == sorted([f"{m}.{a}" for m, a, _ in plugin._BINDINGS] + indexed)
         for module_name, attr, replacement in plugin._BINDINGS:
             assert _original(reference, module_name, attr) is replacement
     finally:
         plugin.uninstall(reference)
     for (module_name, attr), value in originals.items():
         assert _original(reference, module_name, attr) is value
+    hybrid = importlib.import_module(f"{reference.__name__}.hybrid")
+    assert hybrid.HybridKVCache.update_residency.__module__ == f"{reference.__name__}.hybrid"
