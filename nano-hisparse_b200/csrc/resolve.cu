@@ -544,22 +544,29 @@ __global__ void __launch_bounds__(kResolveThreads, 1) resolve_cluster_kernel(Res
   cluster_barrier();  // no CTA exits while another may still use its shared memory
 }
 
-// Whether clusters of `size` resolver CTAs (1024 threads, 128 KiB of shared
-// memory each) fit the device, asked once per device and size.
-bool cluster_schedulable(int size) {
+// Shared memory of each CTA of a `size`-CTA cluster holding `total` bytes of
+// scratch: its share of the 4 KiB granules dealt round-robin.
+size_t cluster_part_bytes(size_t total, int size) {
+  const size_t granules = (total + (size_t(1) << kGranuleShift) - 1) >> kGranuleShift;
+  return ((granules + size - 1) / size) << kGranuleShift;
+}
+
+// Whether clusters of `size` resolver CTAs (1024 threads, `part` bytes of
+// shared memory each) fit the device, asked once per device, size and part.
+bool cluster_schedulable(int size, size_t part) {
   static std::mutex lock;
-  static signed char known[64][kMaxCluster + 1];  // 0 unknown, 1 yes, -1 no
+  static signed char known[64][kMaxCluster + 1][64];  // 0 unknown, 1 yes, -1 no
   int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return false;
+  const size_t kib4 = part >> kGranuleShift;  // part in 4 KiB units (< 64: <= 200 KiB)
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64 || kib4 >= 64) return false;
   std::lock_guard<std::mutex> guard(lock);
-  if (known[dev][size] != 0) return known[dev][size] > 0;
-  bool ok = reserve_smem((const void *)resolve_cluster_kernel, size_t(1) << kClusterShift,
-                         "resolve") == HS_OK;
+  if (known[dev][size][kib4] != 0) return known[dev][size][kib4] > 0;
+  bool ok = reserve_smem((const void *)resolve_cluster_kernel, part, "resolve") == HS_OK;
   if (ok) {
     cudaLaunchConfig_t config{};
     config.gridDim = dim3((unsigned)size);
     config.blockDim = dim3(kResolveThreads);
-    config.dynamicSmemBytes = size_t(1) << kClusterShift;
+    config.dynamicSmemBytes = part;
     cudaLaunchAttribute attr{};
     attr.id = cudaLaunchAttributeClusterDimension;
     attr.val.clusterDim.x = (unsigned)size;
@@ -573,15 +580,15 @@ bool cluster_schedulable(int size) {
          clusters > 0;
     cudaGetLastError();
   }
-  known[dev][size] = ok ? 1 : -1;
+  known[dev][size][kib4] = ok ? 1 : -1;
   return ok;
 }
 
-int launch_cluster(const ResolveParams &p, int size, cudaStream_t stream) {
+int launch_cluster(const ResolveParams &p, int size, size_t part, cudaStream_t stream) {
   cudaLaunchConfig_t config{};
   config.gridDim = dim3((unsigned)(p.batch * size));
   config.blockDim = dim3(kResolveThreads);
-  config.dynamicSmemBytes = size_t(1) << kClusterShift;
+  config.dynamicSmemBytes = part;
   config.stream = stream;
   cudaLaunchAttribute attr{};
   attr.id = cudaLaunchAttributeClusterDimension;
@@ -622,10 +629,16 @@ int resolve_common(ResolveParams &p, size_t workspace_bytes, cudaStream_t stream
     p.workspace = nullptr;
   } else if (L.total <= ((size_t)kMaxCluster << kClusterShift)) {
     // too large for one SM: a cluster keeps the scratch in distributed shared
-    // memory (no workspace read or written)
+    // memory (no workspace read or written). Parts of at most 128 KiB (more
+    // SMs per request) unless the batch's clusters would then need more than
+    // one wave of SMs: then the fewest CTAs whose parts fit kResolveSmemLimit.
     int size = 2;  // a power of two: granules are dealt with masks and shifts
     while (((size_t)size << kClusterShift) < L.total) size <<= 1;
-    if (cluster_schedulable(size)) return launch_cluster(p, size, stream);
+    int fewest = 2;
+    while (fewest < size && cluster_part_bytes(L.total, fewest) > kResolveSmemLimit) fewest <<= 1;
+    if ((int64_t)p.batch * size > sm_count() && fewest < size) size = fewest;
+    const size_t part = cluster_part_bytes(L.total, size);
+    if (cluster_schedulable(size, part)) return launch_cluster(p, size, part, stream);
     const size_t need = hs_resolve_workspace_bytes(p.batch, p.count, p.hot_rows);
     if (!p.workspace || workspace_bytes < need)
       return set_error(HS_ERR_WORKSPACE, "resolve: workspace of %zu bytes < required %zu",

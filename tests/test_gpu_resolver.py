@@ -177,3 +177,68 @@ def test_resolver_graph_capture_without_cpu_readback():
                               case["hot"].numpy(), tags_before, lru_before, 256, 4)
     assert result.counts.tolist() == ref["counts"].tolist()
     assert result.physical_rows.tolist() == ref["physical"].tolist()
+
+
+@pytest.mark.parametrize("batch", [8, 48])
+def test_batched_cluster_forms_against_oracle(batch):
+    """hs_resolve_rows_batched at configuration-3 size (4096 positions, 8192
+    hot rows: scratch for a cluster of CTAs). A batch of 8 runs clusters of 4
+    CTAs; 48 requests would need more than one wave of those, so they run
+    clusters of 2 with larger parts. Every request equals the oracle."""
+    k, h, p, length = 4096, 8192, 16, 131072
+    rng = np.random.default_rng(batch)
+    cases = [_random_case(rng, k, h, p, length) for _ in range(batch)]
+    for c in cases:  # Quest-like input: sorted, -1 padded
+        pos = np.sort(c["positions"].numpy())
+        c["positions"] = torch.tensor(np.where((pos >= 0) & (pos < length), pos, -1),
+                                      dtype=torch.int32)
+        c["positions"] = torch.cat([c["positions"][c["positions"] >= 0],
+                                    c["positions"][c["positions"] < 0]])
+    n = max(len(c["source"]) for c in cases)
+
+    def table(name, dtype, size):
+        out = []
+        for c in cases:
+            t = torch.full((size,), -1, dtype=dtype)
+            t[:len(c[name])] = c[name].to(dtype)
+            out.append(t.to(DEV))
+        return out
+
+    src, res = table("source", torch.int32, n), table("resident", torch.int32, n)
+    hot = [c["hot"].to(torch.int32).to(DEV) for c in cases]
+    tags = [c["tags"].to(torch.int32).to(DEV) for c in cases]
+    lru = [c["lru"].to(DEV) for c in cases]
+
+    def ptrs(ts):
+        return torch.tensor([t.data_ptr() for t in ts], dtype=torch.int64, device=DEV)
+
+    positions = torch.stack([c["positions"] for c in cases]).to(DEV).contiguous()
+    lengths = torch.full((batch,), length, dtype=torch.int32, device=DEV)
+    phys = torch.empty((batch, k), dtype=torch.int64, device=DEV)
+    mh, md = torch.empty_like(phys), torch.empty_like(phys)
+    counts = torch.empty((batch, 3), dtype=torch.int64, device=DEV)
+    lib = _lib.load()
+    ws_bytes = lib.hs_resolve_workspace_bytes(batch, k, h)
+    ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=DEV)
+    status = _lib.status_word(torch.device(DEV))
+    hot_blocks = len(cases[0]["hot"])
+    # the pointer arrays stay referenced until the kernel has read them
+    arrays = [ptrs(x) for x in (src, res, hot, tags, lru)]
+    _lib.check(lib.hs_resolve_rows_batched(
+        batch, positions.data_ptr(), k, arrays[0].data_ptr(), arrays[1].data_ptr(), n,
+        arrays[2].data_ptr(), hot_blocks, arrays[3].data_ptr(), arrays[4].data_ptr(), h,
+        lengths.data_ptr(), p, phys.data_ptr(), mh.data_ptr(), md.data_ptr(),
+        counts.data_ptr(), None, ws.data_ptr(), ws_bytes, status.data_ptr(),
+        _lib.stream_of(torch.device(DEV))))
+    torch.cuda.synchronize()
+    for b, c in enumerate(cases):
+        ref = oracle.resolve_rows(c["positions"].numpy(), c["source"].numpy(),
+                                  c["resident"].numpy(), c["hot"].numpy(), c["tags"].numpy(),
+                                  c["lru"].numpy(), length, p)
+        assert phys[b].tolist() == ref["physical"].tolist(), b
+        assert mh[b].tolist() == ref["miss_host"].tolist(), b
+        assert md[b].tolist() == ref["miss_device"].tolist(), b
+        assert counts[b].tolist() == ref["counts"].tolist(), b
+        assert tags[b].tolist() == ref["tags"].tolist(), b
+        assert lru[b].tolist() == ref["lru"].tolist(), b
+    assert not _lib.device_flags(DEV)
