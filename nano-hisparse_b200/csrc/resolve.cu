@@ -166,7 +166,8 @@ struct LocalScratch {
 };
 
 constexpr int kClusterShift = 17;   // 128 KiB of scratch per CTA of a cluster
-constexpr int kMaxCluster = 8;      // portable cluster size (a power of two is used)
+constexpr int kPortableCluster = 8;  // largest portable cluster size
+constexpr int kMaxCluster = 16;      // with the non-portable opt-in (powers of two are used)
 constexpr int kGranuleShift = 12;   // 4 KiB granules dealt round-robin to the CTAs
 
 struct ClusterScratch {
@@ -562,6 +563,9 @@ bool cluster_schedulable(int size, size_t part) {
   std::lock_guard<std::mutex> guard(lock);
   if (known[dev][size][kib4] != 0) return known[dev][size][kib4] > 0;
   bool ok = reserve_smem((const void *)resolve_cluster_kernel, part, "resolve") == HS_OK;
+  if (ok && size > kPortableCluster)
+    ok = cudaFuncSetAttribute((const void *)resolve_cluster_kernel,
+                              cudaFuncAttributeNonPortableClusterSizeAllowed, 1) == cudaSuccess;
   if (ok) {
     cudaLaunchConfig_t config{};
     config.gridDim = dim3((unsigned)size);
@@ -627,7 +631,7 @@ int resolve_common(ResolveParams &p, size_t workspace_bytes, cudaStream_t stream
   if (L.total <= kResolveSmemLimit) {
     smem = L.total;
     p.workspace = nullptr;
-  } else if (L.total <= ((size_t)kMaxCluster << kClusterShift)) {
+  } else if (L.total <= ((size_t)kPortableCluster << kClusterShift)) {
     // too large for one SM: a cluster keeps the scratch in distributed shared
     // memory (no workspace read or written). Parts of at most 128 KiB (more
     // SMs per request) unless the batch's clusters would then need more than
@@ -637,6 +641,12 @@ int resolve_common(ResolveParams &p, size_t workspace_bytes, cudaStream_t stream
     int fewest = 2;
     while (fewest < size && cluster_part_bytes(L.total, fewest) > kResolveSmemLimit) fewest <<= 1;
     if ((int64_t)p.batch * size > sm_count() && fewest < size) size = fewest;
+    // the largest scratch (clusters of 8) on few requests: 16 CTAs a request
+    // where the device schedules them (one request's resolve is latency-bound,
+    // and more CTAs shorten each of its passes)
+    if (size == kPortableCluster && (int64_t)p.batch * kMaxCluster <= sm_count() &&
+        cluster_schedulable(kMaxCluster, cluster_part_bytes(L.total, kMaxCluster)))
+      size = kMaxCluster;
     const size_t part = cluster_part_bytes(L.total, size);
     if (cluster_schedulable(size, part)) return launch_cluster(p, size, part, stream);
     const size_t need = hs_resolve_workspace_bytes(p.batch, p.count, p.hot_rows);
