@@ -1266,6 +1266,9 @@ def cpu_sample(seed=1, budget_s=10.0, threads=None, log=print):
         "sample": f"{len(times)} layer passes of {REQUESTS} requests (first untimed warm-up), "
                   f"{per_layer * 1e3:.1f} ms per layer, extrapolated x{LAYERS} layers; oracle "
                   "restatement in C (OpenMP over requests; fp64 attention)",
+        "note": "a C port of the reference's per-layer path, batched over the requests, not "
+                "the reference's own torch code: the reference is Python and does not travel "
+                "to the GPU box, and its torch CPU path (one request at a time) is slower still",
     }
 
 
