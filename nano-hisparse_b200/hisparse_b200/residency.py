@@ -175,11 +175,26 @@ class _PinnedView(dict):
     def keys(self):
         return self._real.keys()
 
+    # writes go to the real mapping too (resolve makes none)
+    def __setitem__(self, key, value):
+        self._real[key] = value
+
+    def __delitem__(self, key):
+        del self._real[key]
+
+    def pop(self, key, *default):
+        return self._real.pop(key, *default)
+
+    def setdefault(self, key, default=None):
+        return self._real.setdefault(key, default)
+
 
 def _make_resolve(original):
     """resolve (hybrid.py:412-469) with its page scan answered by the index:
     the reference's method runs unchanged against a view of storage.pages
-    whose values() are the layer's resident pages."""
+    whose values() are the layer's resident pages. The view is in place only
+    for the call, on the calling thread's cache object; like the reference's
+    cache, a cache is not to be used from two threads at once."""
     def resolve(self, request_id, layer, topk):
         storage = self.storage
         real = storage.pages
