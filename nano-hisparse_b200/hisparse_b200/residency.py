@@ -40,40 +40,80 @@ _generation = 0  # bumped by every install/uninstall: an older index is stale
 _saved: dict = {}
 
 
-def _index(allocator) -> dict:
-    """(request, layer) -> {page key: slot} in the allocator's LRU order,
-    built from the LRU on first use after an install."""
+def _state(allocator):
+    """(resident, pinned): (request, layer) -> {page key: slot}. `resident`
+    holds the layer's resident pages in the allocator's LRU order; `pinned`
+    those whose block still holds its allocation reference (not in the
+    allocator's reclaimable set). Built from the allocator on first use
+    after an install, and rebuilt when the reclaimable set's size is not the
+    one the hooks account for (a caller that edits it directly, as one of the
+    reference's policy tests does to re-pin a block)."""
     state = allocator.__dict__.get("_hs_group_index")
-    if state is None or state[0] != _generation:
-        groups: dict = {}
+    if (state is None or state[0] != _generation
+            or state[3][0] != len(allocator.reclaimable)):
+        resident: dict = {}
+        pinned: dict = {}
         for key, slot in allocator.lru.items():
             if key[2] >= 0:
-                groups.setdefault(key[:2], {})[key] = slot
-        state = (_generation, groups)
+                resident.setdefault(key[:2], {})[key] = slot
+                if slot not in allocator.reclaimable:
+                    pinned.setdefault(key[:2], {})[key] = slot
+        state = (_generation, resident, pinned, [len(allocator.reclaimable)])
         allocator.__dict__["_hs_group_index"] = state
-    return state[1]
+    return state[1], state[2]
+
+
+def _count_reclaimable(allocator, delta):
+    allocator.__dict__["_hs_group_index"][3][0] += delta
+
+
+def _index(allocator) -> dict:
+    return _state(allocator)[0]
+
+
+def _drop(index, key):
+    group = index.get(key[:2])
+    if group is not None:
+        group.pop(key, None)
+        if not group:
+            del index[key[:2]]
 
 
 def _make_bind(original):
     def bind(self, slot, key):
         original(self, slot, key)
         if key[2] >= 0:
-            _index(self).setdefault(key[:2], {})[key] = slot
+            resident, pinned = _state(self)
+            resident.setdefault(key[:2], {})[key] = slot
+            pinned.setdefault(key[:2], {})[key] = slot  # bound with its allocation reference
     return bind
 
 
 def _make_release(original):
     def release(self, slot, fence):
         key = self.slots[slot].owner
-        index = _index(self)
+        resident, pinned = _state(self)
+        was = slot in self.reclaimable
         original(self, slot, fence)
+        if was:
+            _count_reclaimable(self, -1)
         if key is not None and key[2] >= 0:
-            group = index.get(key[:2])
-            if group is not None:
-                group.pop(key, None)
-                if not group:
-                    del index[key[:2]]
+            _drop(resident, key)
+            _drop(pinned, key)
     return release
+
+
+def _make_unpin(original):
+    def unpin(self, slot, on_reuse):
+        _, pinned = _state(self)
+        was = slot in self.reclaimable
+        original(self, slot, on_reuse)
+        if not was and slot in self.reclaimable:
+            _count_reclaimable(self, 1)
+        key = self.slots[slot].owner
+        if key is not None and key[2] >= 0:
+            _drop(pinned, key)  # now reclaimable
+    return unpin
 
 
 def resident_keys(cache, group):
@@ -86,6 +126,11 @@ def historical_pages(self, group=None):
     write tail, in allocator LRU order; for one group, walks only that
     group's resident keys."""
     keys = self.allocator.lru if group is None else list(resident_keys(self, group))
+    return _historical_of(self, keys, group)
+
+
+def _historical_of(self, keys, group):
+    """The historical-page filter of hybrid.py:208-222 over `keys`."""
     storage, allocator = self.storage, self.allocator
     found = []
     for key in keys:
@@ -100,6 +145,26 @@ def historical_pages(self, group=None):
                 and key[2] <= tail - self._hs_tail_pages:
             found.append(page)
     return found
+
+
+def unpin_clean_pages(self, group):
+    """hybrid.py:237-247 — unpin, tail first, the layer's clean historical
+    pages that still hold their allocation reference. Only pinned pages can
+    be unpinned, so the candidates are taken from the layer's pinned pages
+    (the reference takes every historical page and skips the reclaimable
+    ones): the same pages in the same order."""
+    if not self.tables[group].blocks:
+        return
+    pinned = _state(self.allocator)[1].get(group)
+    if not pinned:
+        return
+    candidates = _historical_of(self, list(pinned), group)
+    reclaimable = self.allocator.reclaimable
+    for page in sorted(candidates, key=lambda p: -p.key[2]):
+        if (page.host_committed_version == page.content_version
+                and page.slot not in reclaimable):
+            self.allocator.unpin(page.slot, self._on_block_reused)
+            self.storage.stats["clean_page_unpins"] += 1
 
 
 def update_residency(self, request_id=None, layer=None, *, upcoming_allocation=False):
@@ -219,7 +284,9 @@ def install(package) -> list[str]:
     replacements = [
         (alloc_cls, "bind", _make_bind),
         (alloc_cls, "release", _make_release),
+        (alloc_cls, "unpin", _make_unpin),
         (cache_cls, "_historical_pages", lambda original: historical_pages),
+        (cache_cls, "_unpin_clean_pages", lambda original: unpin_clean_pages),
         (cache_cls, "update_residency", lambda original: update_residency),
         (cache_cls, "resolve", _make_resolve),
     ]

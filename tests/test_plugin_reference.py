@@ -126,9 +126,9 @@ def test_install_and_uninstall_on_the_reference(reference):
     originals = {(m, a): _original(reference, m, a) for m, a, _ in plugin._BINDINGS}
     bound = plugin.install(reference)
     try:
-        indexed = ["DeviceAllocator.bind", "DeviceAllocator.release",
-                   "HybridKVCache._historical_pages", "HybridKVCache.update_residency",
-                   "HybridKVCache.resolve"]
+        indexed = ["DeviceAllocator.bind", "DeviceAllocator.release", "DeviceAllocator.unpin",
+                   "HybridKVCache._historical_pages", "HybridKVCache._unpin_clean_pages",
+                   "HybridKVCache.update_residency", "HybridKVCache.resolve"]
         assert sorted(bound) == sorted([f"{m}.{a}" for m, a, _ in plugin._BINDINGS] + indexed)
         for module_name, attr, replacement in plugin._BINDINGS:
             assert _original(reference, module_name, attr) is replacement

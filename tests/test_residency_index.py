@@ -1,10 +1,11 @@
 """Indexed residency control against the REAL reference (CPU; skipped where
 the reference checkout is absent, e.g. on a GPU box).
 
-hisparse_b200.residency replaces three scans of the reference's
+hisparse_b200.residency replaces four scans of the reference's
 HybridKVCache (resolve's page pinning, update_residency's resident count,
-_historical_pages per layer; hybrid.py:204-296, 412-469) with a per-layer
-index kept beside the allocator's LRU. The policy must not change: the
+_historical_pages and _unpin_clean_pages per layer; hybrid.py:204-296,
+412-469) with per-layer indexes of resident and of pinned pages kept beside
+the allocator. The policy must not change: the
 reference's own test suite passes with the index installed, and scripted
 random sessions (appends, sparse attention with reuse, reclaim, hot
 transitions, capacity pressure, releases) give identical outputs, counters,
@@ -53,6 +54,7 @@ def test_reference_suite_passes_with_the_index():
     assert result.returncode == 0, tail
     assert " passed" in result.stdout and "failed" not in result.stdout, tail
     assert "indexed residency installed: DeviceAllocator.bind" in result.stdout, tail
+    assert "HybridKVCache._unpin_clean_pages" in result.stdout, tail
 
 
 def _state(cache):
@@ -147,6 +149,8 @@ def _index_matches_scan(cache):
         resident = [p.key for p in cache.storage.pages.values()
                     if p.key[:2] == group and p.slot is not None]
         assert sorted(resident) == sorted(scanned)
+        pinned = [k for k in scanned if cache.allocator.lru[k] not in cache.allocator.reclaimable]
+        assert sorted(residency._state(cache.allocator)[1].get(group, {})) == sorted(pinned)
 
 
 @pytest.mark.parametrize("seed", range(12))
